@@ -1,0 +1,368 @@
+#!/usr/bin/env python
+"""Benchmark of the attention hot path on B200 (one JSON line on rank 0).
+
+Headline workload ("batched GQA decode"): per GPU, 32 sequences with context
+lengths uniform in [1024, 32768] (seed 0), 16 query / 2 KV heads, head_dim 256, fp16 KV cache
+N(0, 1), fp32 queries and gate logits N(0, 1). One step = one decode token for every sequence:
+batched prep (RMSNorm + RoPE + KV append, lens advance) then the stream-K split-K decode with
+the gated combine fused in. Metric: decode tokens/s (whole job), with the decode kernel's HBM
+GB/s against the measured HBM peak.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl miso|reference]
+
+Multi-GPU: one process per GPU under torchrun; each rank decodes its own batch of 32
+(independent sequences, no collective on the data path: weak scaling); the step time is the
+max over ranks of device-event time.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+BATCH = 32
+LEN_LO, LEN_HI = 1024, 32768
+Q_HEADS, KV_HEADS, DIM = 16, 2, 256
+PROJ = 9216  # per-token projection row [q+gate 8192 | k 512 | v 512]
+EPS = 1e-6
+KV_BYTES_PER_POS = KV_HEADS * DIM * 2 * 2  # K and V, fp16: 2048 B per position
+QGO_BYTES_PER_SEQ = 3 * Q_HEADS * DIM * 4  # q read, gate read, core written
+
+
+def lens_config() -> np.ndarray:
+    return np.random.RandomState(0).randint(LEN_LO, LEN_HI + 1, size=BATCH).astype(np.int32)
+
+
+def peaks() -> dict:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        d = json.load(open(path))
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "source": "measured (MEASURED_PEAKS.json)"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+class Clocks:
+    """Samples nvidia-smi clocks / throttle reasons while the timed region runs."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.p is not None:
+            self.p.terminate()
+            try:
+                self.p.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.p.kill()
+
+    def summary(self) -> dict:
+        self.f.flush()
+        rows = []
+        for line in open(self.f.name):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ------------------------------------------------------------------------------- reference arm
+
+
+def cpu_decode_sample(lens: np.ndarray, seqs: list[int], seed: int, threads: int):
+    """Host data for a sample of sequences and a callable that runs the oracle decode on it."""
+    import oracle
+    rng = np.random.RandomState(seed)
+    sub = lens[seqs]
+    cap = int(sub.max())
+    rows = len(seqs) * KV_HEADS * cap
+    k = rng.standard_normal((rows, DIM)).astype(np.float16).view(np.uint16)
+    v = rng.standard_normal((rows, DIM)).astype(np.float16).view(np.uint16)
+    kv_row = (np.arange(len(seqs) * KV_HEADS, dtype=np.int64) * cap).reshape(-1, KV_HEADS)
+    q = rng.standard_normal((len(seqs), Q_HEADS, DIM)).astype(np.float32)
+    qg = rng.standard_normal((len(seqs), Q_HEADS, 2 * DIM)).astype(np.float32)
+    return lambda: oracle.attn_decode(q, qg, Q_HEADS * 2 * DIM, k, v, kv_row, sub,
+                                      threads=threads)
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import oracle
+    oracle.build()
+    threads = oracle.cpu_count()
+    lens = lens_config()
+    per_step = 4  # sequences per step: a bounded sample of the batch
+    steps = []
+    for i in range(args.warmup + args.steps):
+        seqs = [(i * per_step + j) % BATCH for j in range(per_step)]
+        fn = cpu_decode_sample(lens, seqs, seed=100 + i, threads=threads)
+        t0 = time.perf_counter()
+        fn()
+        dt = time.perf_counter() - t0
+        if i >= args.warmup:
+            steps.append(dt)
+    t = sum(steps) / len(steps)
+    value = per_step / t
+    line = {
+        "impl": "reference", "metric": "attn decode tok/s", "value": value, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * t, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": workload_config(args.gpus),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"{per_step} of the {BATCH} sequences per step (rotating), "
+                                   "fp64 restatement of the reference's decode reference"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(n_gpus: int) -> dict:
+    return {"workload": "batched GQA decode (BASELINE config 2)", "batch_per_gpu": BATCH,
+            "global_batch": BATCH * n_gpus, "ctx_len": f"U[{LEN_LO}, {LEN_HI}] seed 0",
+            "mean_ctx": float(lens_config().mean()), "q_heads": Q_HEADS, "kv_heads": KV_HEADS,
+            "head_dim": DIM, "kv_dtype": "fp16", "q_dtype": "fp32",
+            "parallelism": f"dp{n_gpus} (independent sequences per GPU)",
+            "l2": "inputs larger than L2 (KV stream ~1.1 GB per step per GPU)"}
+
+
+# ------------------------------------------------------------------------------------- miso arm
+
+
+def run_miso(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=dev)
+
+    import miso_b200
+    from miso_b200 import attention as A
+    from miso_b200 import capi
+
+    lens0 = lens_config()
+    extra = args.warmup + 2 * args.steps + 4  # room for the appended tokens
+    caps = (lens0.astype(np.int64) + extra)
+    seg_caps = np.repeat(caps, KV_HEADS)
+    starts = np.concatenate([[0], np.cumsum(seg_caps)[:-1]]).astype(np.int64)
+    rows = int(seg_caps.sum())
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+    pool = A.KvPool.__new__(A.KvPool)
+    pool.batch, pool.capacity, pool.rows = BATCH, None, rows
+    pool.k = torch.randn((rows, DIM), generator=g, device=dev, dtype=torch.float16)
+    pool.v = torch.randn((rows, DIM), generator=g, device=dev, dtype=torch.float16)
+    pool.kv_row = torch.from_numpy(starts.reshape(BATCH, KV_HEADS)).to(dev)
+    pool.lens = torch.from_numpy(lens0.copy()).to(dev)
+
+    proj = torch.randn((BATCH, PROJ), generator=g, device=dev, dtype=torch.float32)
+    q_norm = (1.0 + 0.1 * torch.randn(DIM, generator=g, device=dev)).float()
+    k_norm = (1.0 + 0.1 * torch.randn(DIM, generator=g, device=dev)).float()
+    inv_freq = torch.from_numpy(A.rope_inv_freq()).to(dev)
+    q = torch.empty((BATCH, Q_HEADS, DIM), device=dev)
+    core = torch.empty((BATCH, Q_HEADS, DIM), device=dev)
+    scratch = A.decode_scratch(BATCH, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    base = proj.data_ptr()
+
+    def step(src_base: int):
+        p = capi.AttnPrepBatchedParams(src_base, src_base + 8192 * 4, src_base + 8704 * 4,
+                                       q_norm.data_ptr(), k_norm.data_ptr(), inv_freq.data_ptr(),
+                                       pool.k.data_ptr(), pool.v.data_ptr(),
+                                       pool.kv_row.data_ptr(), pool.lens.data_ptr(),
+                                       q.data_ptr(), BATCH, PROJ, EPS)
+        capi.check("miso_attn_prep_batched",
+                   capi.load().miso_attn_prep_batched(ctypes.byref(p),
+                                                      stream.cuda_stream))
+
+    def decode(qg_base: int):
+        dp = capi.AttnDecodeParams(q.data_ptr(), qg_base, pool.k.data_ptr(), pool.v.data_ptr(),
+                                   pool.kv_row.data_ptr(), pool.lens.data_ptr(), core.data_ptr(),
+                                   rows, BATCH, PROJ)
+        capi.check("miso_attn_decode",
+                   capi.load().miso_attn_decode(ctypes.byref(dp),
+                                                scratch.data_ptr(),
+                                                scratch.numel() * 4, stream.cuda_stream))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident timing ---------------------------------------------------------------
+    for _ in range(args.warmup):
+        step(base)
+        decode(base)
+    torch.cuda.synchronize()
+    lens_start = pool.lens.cpu().numpy().astype(np.int64)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        start.record(stream)
+        for i in range(args.steps):
+            step(base)
+            ev[i][0].record(stream)
+            decode(base)
+            ev[i][1].record(stream)
+        end.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    step_ms = start.elapsed_time(end) / args.steps
+    dec_ms = [a.elapsed_time(b) for a, b in ev]
+    step_ms_max = max_over_ranks(step_ms)
+    # Algorithmic bytes of each decode launch: every position of every sequence, K and V, plus
+    # q / gate reads and the output write.
+    dec_bytes = [float(((lens_start + i + 1) * KV_BYTES_PER_POS).sum() + BATCH * QGO_BYTES_PER_SEQ)
+                 for i in range(args.steps)]
+    dec_avg_ms = sum(dec_ms) / len(dec_ms)
+    achieved = (sum(dec_bytes) / len(dec_bytes)) / (dec_avg_ms * 1e-3) / 1e9
+    pk = peaks()
+
+    # ---- end to end through the C ABI with host buffers ---------------------------------------
+    host_in = torch.randn((BATCH, PROJ), dtype=torch.float32).pin_memory()
+    host_out = torch.empty((BATCH, Q_HEADS, DIM), dtype=torch.float32).pin_memory()
+    dev_in = torch.empty((BATCH, PROJ), device=dev)
+    for _ in range(args.warmup):
+        dev_in.copy_(host_in, non_blocking=True)
+        step(dev_in.data_ptr())
+        decode(dev_in.data_ptr())
+        host_out.copy_(core, non_blocking=True)
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        dev_in.copy_(host_in, non_blocking=True)
+        step(dev_in.data_ptr())
+        decode(dev_in.data_ptr())
+        host_out.copy_(core, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+
+    st = ctypes.c_int(-1)
+    capi.check("miso_device_status", capi.load().miso_device_status(1, st))
+    if st.value != 0:
+        raise RuntimeError(f"device status {st.value} after the timed region")
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        import oracle
+        oracle.build()
+        threads = oracle.cpu_count()
+        per = 8
+        fn = cpu_decode_sample(lens0, list(range(per)), seed=7, threads=threads)
+        fn()
+        t0 = time.perf_counter()
+        reps = 0
+        while True:
+            fn()
+            reps += 1
+            if time.perf_counter() - t0 > 10.0 or reps >= 20:
+                break
+        t = (time.perf_counter() - t0) / reps
+        cpu = {"value": per / t, "unit": "tokens/s", "cores": threads, "kind": "port",
+               "sample": f"sequences 0-{per - 1} of the batch (lens {int(lens0[:per].min())}-"
+                         f"{int(lens0[:per].max())}), {reps} repetitions, fp64 restatement of "
+                         "the reference decode (tests/test_attn_splitk.hip:153-173)"}
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    value = world * BATCH / (step_ms_max * 1e-3)
+    line = {
+        "metric": "attn decode tok/s", "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms_max,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16kv-f32",
+        "data": "synthetic", "config": workload_config(world),
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"],
+                     "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "traffic": None,
+                     "kernel": "decode_kernel", "kernel_ms": dec_avg_ms,
+                     "peak_source": pk["source"]},
+        "e2e": {"value": world * BATCH / (e2e_ms * 1e-3), "unit": "tokens/s",
+                "h2d_bytes_per_step": BATCH * PROJ * 4,
+                "d2h_bytes_per_step": BATCH * Q_HEADS * DIM * 4},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clk.summary(),
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["miso", "reference"], default="miso")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_miso(args)
+
+
+if __name__ == "__main__":
+    main()

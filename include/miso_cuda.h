@@ -1,0 +1,280 @@
+/*
+ * miso_cuda.h — C ABI of the B200 (sm_100a) attention hot path.
+ *
+ * Plain C: device pointers, sizes and an opaque stream. No C++ or framework types cross this
+ * boundary, so it binds directly from C, C++ (the engine), Python ctypes or any other FFI.
+ *
+ * Conventions
+ *   - Every pointer named in a params struct is a DEVICE pointer unless its comment says host.
+ *   - `stream` is a cudaStream_t passed as void*; NULL is the legacy default stream.
+ *   - Calls only enqueue work; none synchronises the host (except miso_device_status).
+ *   - Return value: MISO_OK (0) on success; a negative MISO_ERR_* for a rejected argument (nothing
+ *     was launched); a positive value is the cudaError_t reported by the launch.
+ *   - The params structs are layout-identical to the reference's POD Params structs
+ *     (miso::kernels::*Params in the drop-in headers; fp16 pointers appear here as uint16_t*),
+ *     so a caller can pass a pointer to its existing Params object.
+ *
+ * Shapes are fixed by the model (Qwen3.5-MoE hybrid attention): 16 query heads, 2 KV heads,
+ * head_dim 256, partial RoPE over the first 64 dims; DeltaNet 16 K heads, 32 V heads, d = 128.
+ */
+#ifndef MISO_CUDA_H
+#define MISO_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MISO_ATTN_Q_HEADS 16
+#define MISO_ATTN_KV_HEADS 2
+#define MISO_ATTN_DIM 256
+#define MISO_ATTN_ROPE_DIM 64
+#define MISO_ATTN_SUB_CHUNK 32 /* kAttnSubChunk, kernels/attention_decode.hpp:90 */
+#define MISO_ATTN_Q_BLOCK 4    /* kAttnQBlock, kernels/attention_prefill.hpp:52 */
+#define MISO_DN_K_HEADS 16
+#define MISO_DN_V_HEADS 32
+#define MISO_DN_DIM 128
+#define MISO_DN_CHUNK 64 /* kDeltaChunk, kernels/deltanet_chunk.hpp:22 */
+
+enum {
+  MISO_OK = 0,
+  MISO_ERR_INVALID = -1,   /* null pointer, size out of range or misaligned buffer */
+  MISO_ERR_SCRATCH = -2,   /* scratch buffer smaller than the *_scratch_bytes() figure */
+  MISO_ERR_NO_DEVICE = -3, /* no CUDA device, or not an sm_100 device */
+  MISO_ERR_DRIVER = -4     /* a driver entry point (tensor-map encoding) was unavailable */
+};
+
+/* Device status word (miso_device_status). */
+enum { MISO_STATUS_OK = 0, MISO_STATUS_TIMEOUT = 1 };
+
+/* ---------------------------------------------------------------------------------------------
+ * Drop-in family: one entry point per reference __global__, same Params, same launch geometry
+ * as the reference engine uses, same semantics.
+ * ------------------------------------------------------------------------------------------- */
+
+/* == miso::kernels::AttnPrepParams, kernels/attention_decode.hpp:19-31. */
+typedef struct {
+  const float* qg;       /* [16][512]: per head 256 query then 256 gate */
+  const float* k;        /* [2][256] */
+  const float* v;        /* [2][256] */
+  const float* q_norm;   /* [256] (stores 1 + w) */
+  const float* k_norm;   /* [256] */
+  const float* inv_freq; /* [32] */
+  uint16_t* k_cache;     /* fp16 [2][max_ctx][256] */
+  uint16_t* v_cache;     /* fp16 [2][max_ctx][256] */
+  float* q;              /* [16][256] normalised, rotated queries */
+  unsigned pos, max_ctx;
+  float eps;
+} miso_attn_prep_params;
+
+/* == miso::kernels::AttnPrepBatchParams, kernels/attention_decode.hpp:35-39. */
+typedef struct {
+  miso_attn_prep_params tok0;
+  unsigned n;
+  unsigned proj_stride;
+} miso_attn_prep_batch_params;
+
+/* == miso::kernels::AttnSplitParams, kernels/attention_decode.hpp:117-125. */
+typedef struct {
+  const float* q; /* [16][256] (unscaled) */
+  const uint16_t* k_cache;
+  const uint16_t* v_cache;
+  float* part_m; /* [2][n_splits][8] */
+  float* part_l; /* [2][n_splits][8] */
+  float* part_o; /* [2][n_splits][8][256] */
+  unsigned len, max_ctx, n_splits;
+} miso_attn_split_params;
+
+/* == miso::kernels::AttnCombineParams, kernels/attention_decode.hpp:238-245. */
+typedef struct {
+  const float* part_m;
+  const float* part_l;
+  const float* part_o;
+  const float* qg; /* [16][512], gate half */
+  float* core;     /* [16][256] */
+  unsigned n_splits;
+} miso_attn_combine_params;
+
+/* == miso::kernels::AttnPrefillParams, kernels/attention_prefill.hpp:42-50. */
+typedef struct {
+  const float* q;  /* [n][16][256] normalised, rotated (unscaled) */
+  const float* qg; /* gate at tok * qg_stride + head * 512 + 256 */
+  const uint16_t* k_cache;
+  const uint16_t* v_cache;
+  float* core; /* [n][16][256] */
+  unsigned pos0, n, max_ctx;
+  unsigned qg_stride;
+} miso_attn_prefill_params;
+
+/* == miso::kernels::DeltaNetStepParams, kernels/deltanet_step.hpp:22-36. */
+typedef struct {
+  const float* qkv;     /* [8192]: q[2048] k[2048] v[4096] */
+  const float* z;       /* [4096] */
+  const float* a;       /* [32] */
+  const float* b;       /* [32] */
+  const float* conv_w;  /* [8192][4] */
+  const float* conv_in; /* [8192][3] */
+  float* conv_out;      /* [8192][3] */
+  const float* ssm_a;   /* [32] */
+  const float* dt_bias; /* [32] */
+  const float* norm_w;  /* [128] */
+  float* state;         /* [32][128 k][128 v] */
+  float* out;           /* [4096] */
+  float eps;
+} miso_deltanet_step_params;
+
+/* == miso::kernels::DeltaNetSeqParams, kernels/deltanet_step.hpp:146-163. */
+typedef struct {
+  const float* qkv; /* [n][qkv_stride] */
+  const float* z;   /* [n][zab_stride] */
+  const float* a;
+  const float* b;
+  const float* conv_w;
+  const float* conv_in;
+  float* conv_out;
+  const float* ssm_a;
+  const float* dt_bias;
+  const float* norm_w;
+  float* state;
+  float* out; /* [n][4096] */
+  unsigned n;
+  float eps;
+  unsigned zab_stride;
+  unsigned qkv_stride;
+} miso_deltanet_seq_params;
+
+/* == miso::kernels::DeltaNetConvParams, kernels/deltanet_chunk.hpp:24-39. */
+typedef struct {
+  const float* qkv; /* [n][8192] */
+  const float* a;   /* [n][32] */
+  const float* b;   /* [n][32] */
+  const float* conv_w;
+  const float* conv_in;
+  float* conv_out;
+  const float* ssm_a;
+  const float* dt_bias;
+  float* q;     /* [n][16][128] */
+  float* k;     /* [n][16][128] */
+  float* v;     /* [n][32][128] */
+  float* beta;  /* [n][32] */
+  float* log_a; /* [n][32] */
+  unsigned n;
+} miso_deltanet_conv_params;
+
+/* == miso::kernels::DeltaNetChunkParams, kernels/deltanet_chunk.hpp:114-128. */
+typedef struct {
+  const float* q;
+  const float* k;
+  const float* v;
+  const float* beta;
+  const float* log_a;
+  const float* z; /* [n][4096] */
+  const float* norm_w;
+  float* state; /* [32][128][128] */
+  float* out;   /* [n][4096] */
+  float* sk;    /* [32][64][128] scratch */
+  float* sq;    /* [32][64][128] scratch */
+  unsigned n;
+  float eps;
+} miso_deltanet_chunk_params;
+
+/* attn_n_splits, kernels/attention_decode.hpp:95-115 (host function, pure). */
+unsigned miso_attn_n_splits(unsigned len, unsigned max_splits);
+/* attn_prefill_items, kernels/attention_prefill.hpp:54-56 (host function, pure). */
+unsigned miso_attn_prefill_items(unsigned n);
+
+/* attn_prep_kernel<256><<<18, 256>>>, launched at src/engine/attention.hip:100. */
+int miso_attn_prep(const miso_attn_prep_params* p, void* stream);
+/* attn_prep_batch_kernel<256><<<n * 18, 256>>>, src/engine/attention.hip:140. */
+int miso_attn_prep_batch(const miso_attn_prep_batch_params* p, void* stream);
+/* attn_split_kernel<256><<<(n_splits, 2), 256>>>, src/engine/attention.hip:106. */
+int miso_attn_split(const miso_attn_split_params* p, void* stream);
+/* attn_combine_kernel<64, true, 4><<<64, 64>>>, src/engine/attention.hip:109. */
+int miso_attn_combine(const miso_attn_combine_params* p, void* stream);
+/* attn_prefill_kernel<256><<<attn_prefill_items(n), 256>>>, src/engine/attention.hip:144. */
+int miso_attn_prefill(const miso_attn_prefill_params* p, void* stream);
+/* deltanet_step_kernel<256><<<32, 256>>>, src/engine/deltanet.hip:79. */
+int miso_deltanet_step(const miso_deltanet_step_params* p, void* stream);
+/* deltanet_seq_kernel<256><<<32, 256>>>, src/engine/deltanet.hip:113. */
+int miso_deltanet_seq(const miso_deltanet_seq_params* p, void* stream);
+/* deltanet_conv_kernel<<<32, 256>>>, tests/test_deltanet_chunk.hip:82. */
+int miso_deltanet_conv(const miso_deltanet_conv_params* p, void* stream);
+/* deltanet_norm_kernel<<<64, 256>>>, tests/test_deltanet_chunk.hip:83. */
+int miso_deltanet_norm(const miso_deltanet_conv_params* p, void* stream);
+/* deltanet_chunk_kernel<256><<<32, 256>>>, tests/test_deltanet_chunk.hip:88. */
+int miso_deltanet_chunk(const miso_deltanet_chunk_params* p, void* stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Fast family: B200-native kernels with library-chosen geometry. No reference counterpart takes
+ * a batch; each replaces a reference launch sequence as noted.
+ * ------------------------------------------------------------------------------------------- */
+
+/* Batched split-K decode over an fp16 KV pool. Replaces the attn_split_kernel +
+ * attn_combine_kernel pair (src/engine/attention.hip:102-109) for `batch` sequences at once.
+ * Sequence b, KV head h occupies pool rows [kv_row[2b+h], kv_row[2b+h] + lens[b]) of k_pool and
+ * v_pool (a reference AttentionCache [2][max_ctx][256] is the case kv_row = {0, max_ctx}).
+ *   core[b][h][d] = softmax(q[b][h] . K^T / 16) V [d] * sigmoid(qg[b * qg_stride + h*512 + 256 + d])
+ * lens[b] == 0 gives core = 0. Work is divided evenly over the SMs by key tiles (stream-K); a
+ * sequence cut across CTAs is merged by the last CTA to finish it, using `scratch`.
+ * scratch: at least miso_attn_decode_scratch_bytes(batch) bytes, ZEROED BEFORE ITS FIRST USE;
+ * every successful call leaves it ready for the next one (calls sharing one scratch buffer must
+ * not overlap in time). Requires batch <= 1024, pool_rows < 2^31, 16-byte aligned pools. */
+typedef struct {
+  const float* q;         /* [batch][16][256] normalised, rotated queries (unscaled) */
+  const float* qg;        /* gate of (b, h, d) at qg[b * qg_stride + h * 512 + 256 + d] */
+  const uint16_t* k_pool; /* fp16 [pool_rows][256] */
+  const uint16_t* v_pool; /* fp16 [pool_rows][256] */
+  const int64_t* kv_row;  /* [batch][2] first pool row of each (sequence, KV head) */
+  const int32_t* lens;    /* [batch] keys per sequence */
+  float* core;            /* [batch][16][256] */
+  uint64_t pool_rows;
+  unsigned batch;
+  unsigned qg_stride;
+} miso_attn_decode_params;
+
+size_t miso_attn_decode_scratch_bytes(unsigned batch);
+int miso_attn_decode(const miso_attn_decode_params* p, void* scratch, size_t scratch_bytes,
+                     void* stream);
+
+/* Batched decode prep: attn_prep_kernel (kernels/attention_decode.hpp:41-83) for `batch`
+ * sequences, each at its own position pos = lens[b]; appends K/V to the pool rows kv_row[2b+h] +
+ * pos and then sets lens[b] = pos + 1 (one CTA per sequence, so there is no race on lens[b]).
+ * Token b's inputs: qg at qg + b*proj_stride ([16][512]), k at k + b*proj_stride ([2][256]),
+ * v at v + b*proj_stride ([2][256]). */
+typedef struct {
+  const float* qg;
+  const float* k;
+  const float* v;
+  const float* q_norm;
+  const float* k_norm;
+  const float* inv_freq;
+  uint16_t* k_pool;
+  uint16_t* v_pool;
+  const int64_t* kv_row; /* [batch][2] */
+  int32_t* lens;         /* [batch], read as the position, then incremented */
+  float* q;              /* [batch][16][256] */
+  unsigned batch;
+  unsigned proj_stride;
+  float eps;
+} miso_attn_prep_batched_params;
+
+int miso_attn_prep_batched(const miso_attn_prep_batched_params* p, void* stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Library state
+ * ------------------------------------------------------------------------------------------- */
+
+/* Reads (and if reset != 0 clears) the device status word of the current device. Synchronises
+ * the device. A kernel that gave up on a bounded wait records MISO_STATUS_TIMEOUT there. */
+int miso_device_status(int reset, int* status);
+
+/* Version string of the built library. */
+const char* miso_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MISO_CUDA_H */

@@ -1,0 +1,361 @@
+// C ABI of the B200 attention hot path (declared in include/miso_cuda.h).
+//
+// Drop-in entry points launch the reference-named kernels of kernels/*.hpp with the geometry the
+// reference engine uses; fast entry points launch the sm_100a kernels of fast/*.cuh with
+// library-chosen geometry. Nothing here throws: every entry point returns MISO_OK, a negative
+// MISO_ERR_* for a rejected argument, or the positive cudaError_t of the launch.
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <mutex>
+
+#include "miso_cuda.h"
+
+#include "common/device.cuh"
+#include "fast/attn_decode.cuh"
+#include "fast/attn_prep.cuh"
+#include "kernels/attention_decode.hpp"
+#include "kernels/attention_prefill.hpp"
+#include "kernels/deltanet_chunk.hpp"
+#include "kernels/deltanet_step.hpp"
+
+namespace k = miso::kernels;
+
+// ---- the C structs are the reference Params, field for field ---------------------------------
+
+#define MISO_SAME_LAYOUT(C, CPP, field) \
+  static_assert(offsetof(C, field) == offsetof(CPP, field), #C "." #field)
+
+static_assert(sizeof(miso_attn_prep_params) == sizeof(k::AttnPrepParams), "AttnPrepParams size");
+MISO_SAME_LAYOUT(miso_attn_prep_params, k::AttnPrepParams, k_cache);
+MISO_SAME_LAYOUT(miso_attn_prep_params, k::AttnPrepParams, q);
+MISO_SAME_LAYOUT(miso_attn_prep_params, k::AttnPrepParams, pos);
+MISO_SAME_LAYOUT(miso_attn_prep_params, k::AttnPrepParams, eps);
+static_assert(sizeof(miso_attn_prep_batch_params) == sizeof(k::AttnPrepBatchParams), "batch");
+MISO_SAME_LAYOUT(miso_attn_prep_batch_params, k::AttnPrepBatchParams, n);
+MISO_SAME_LAYOUT(miso_attn_prep_batch_params, k::AttnPrepBatchParams, proj_stride);
+static_assert(sizeof(miso_attn_split_params) == sizeof(k::AttnSplitParams), "AttnSplitParams");
+MISO_SAME_LAYOUT(miso_attn_split_params, k::AttnSplitParams, part_o);
+MISO_SAME_LAYOUT(miso_attn_split_params, k::AttnSplitParams, n_splits);
+static_assert(sizeof(miso_attn_combine_params) == sizeof(k::AttnCombineParams), "combine");
+MISO_SAME_LAYOUT(miso_attn_combine_params, k::AttnCombineParams, core);
+MISO_SAME_LAYOUT(miso_attn_combine_params, k::AttnCombineParams, n_splits);
+static_assert(sizeof(miso_attn_prefill_params) == sizeof(k::AttnPrefillParams), "prefill");
+MISO_SAME_LAYOUT(miso_attn_prefill_params, k::AttnPrefillParams, core);
+MISO_SAME_LAYOUT(miso_attn_prefill_params, k::AttnPrefillParams, qg_stride);
+static_assert(sizeof(miso_deltanet_step_params) == sizeof(k::DeltaNetStepParams), "step");
+MISO_SAME_LAYOUT(miso_deltanet_step_params, k::DeltaNetStepParams, state);
+MISO_SAME_LAYOUT(miso_deltanet_step_params, k::DeltaNetStepParams, eps);
+static_assert(sizeof(miso_deltanet_seq_params) == sizeof(k::DeltaNetSeqParams), "seq");
+MISO_SAME_LAYOUT(miso_deltanet_seq_params, k::DeltaNetSeqParams, n);
+MISO_SAME_LAYOUT(miso_deltanet_seq_params, k::DeltaNetSeqParams, qkv_stride);
+static_assert(sizeof(miso_deltanet_conv_params) == sizeof(k::DeltaNetConvParams), "conv");
+MISO_SAME_LAYOUT(miso_deltanet_conv_params, k::DeltaNetConvParams, log_a);
+MISO_SAME_LAYOUT(miso_deltanet_conv_params, k::DeltaNetConvParams, n);
+static_assert(sizeof(miso_deltanet_chunk_params) == sizeof(k::DeltaNetChunkParams), "chunk");
+MISO_SAME_LAYOUT(miso_deltanet_chunk_params, k::DeltaNetChunkParams, sq);
+MISO_SAME_LAYOUT(miso_deltanet_chunk_params, k::DeltaNetChunkParams, eps);
+
+namespace {
+
+int launch_status() {
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? MISO_OK : static_cast<int>(e);
+}
+
+cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ---- per-device state ----------------------------------------------------------------------
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceInfo {
+  std::once_flag once;
+  int status = MISO_OK;
+  int sms = 0;
+};
+
+DeviceInfo g_dev[kMaxDevices];
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+int device_info(DeviceInfo** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess)
+    return static_cast<int>(e);
+  if (dev < 0 || dev >= kMaxDevices)
+    return MISO_ERR_NO_DEVICE;
+  DeviceInfo& d = g_dev[dev];
+  std::call_once(d.once, [&] {
+    int major = 0, sms = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+      d.status = MISO_ERR_NO_DEVICE;
+      return;
+    }
+    if (major != 10) {
+      d.status = MISO_ERR_NO_DEVICE;
+      return;
+    }
+    d.sms = sms;
+    const cudaError_t a = cudaFuncSetAttribute(miso::fast::decode::decode_kernel,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(miso::fast::decode::kSmemBytes));
+    d.status = a == cudaSuccess ? MISO_OK : static_cast<int>(a);
+  });
+  *out = &d;
+  return d.status;
+}
+
+int tensor_map_encoder() {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  return g_encode != nullptr ? MISO_OK : MISO_ERR_DRIVER;
+}
+
+// 2-D fp16 map over a [rows][256] pool; box = 64 dims x 64 rows, 128-byte swizzle.
+int kv_pool_map(CUtensorMap* map, const void* pool, uint64_t rows) {
+  const cuuint64_t dims[2] = {256, rows};
+  const cuuint64_t strides[1] = {256 * sizeof(uint16_t)};
+  const cuuint32_t box[2] = {64, 64};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(pool),
+                              dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? MISO_OK : MISO_ERR_INVALID;
+}
+
+size_t decode_counter_bytes(unsigned batch) {
+  return (size_t(2) * batch * sizeof(int) + 255) & ~size_t(255);
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* miso_version(void) { return "miso_b200 0.1 (sm_100a)"; }
+
+unsigned miso_attn_n_splits(unsigned len, unsigned max_splits) {
+  return k::attn_n_splits(len, max_splits);
+}
+
+unsigned miso_attn_prefill_items(unsigned n) { return k::attn_prefill_items(n); }
+
+int miso_device_status(int reset, int* status) {
+  if (status == nullptr)
+    return MISO_ERR_INVALID;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess)
+    return static_cast<int>(e);
+  e = cudaMemcpyFromSymbol(status, miso::dev::g_status, sizeof(int));
+  if (e != cudaSuccess)
+    return static_cast<int>(e);
+  if (reset) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(miso::dev::g_status, &zero, sizeof(int));
+    if (e != cudaSuccess)
+      return static_cast<int>(e);
+  }
+  return MISO_OK;
+}
+
+// ---- drop-in family ---------------------------------------------------------------------------
+
+int miso_attn_prep(const miso_attn_prep_params* p, void* stream) {
+  if (p == nullptr || p->qg == nullptr || p->k == nullptr || p->v == nullptr ||
+      p->q_norm == nullptr || p->k_norm == nullptr || p->inv_freq == nullptr ||
+      p->k_cache == nullptr || p->v_cache == nullptr || p->q == nullptr || p->pos >= p->max_ctx)
+    return MISO_ERR_INVALID;
+  k::attn_prep_kernel<256><<<18, 256, 0, as_stream(stream)>>>(
+      *reinterpret_cast<const k::AttnPrepParams*>(p));
+  return launch_status();
+}
+
+int miso_attn_prep_batch(const miso_attn_prep_batch_params* p, void* stream) {
+  if (p == nullptr || p->tok0.qg == nullptr || p->tok0.k == nullptr || p->tok0.v == nullptr ||
+      p->tok0.q_norm == nullptr || p->tok0.k_norm == nullptr || p->tok0.inv_freq == nullptr ||
+      p->tok0.k_cache == nullptr || p->tok0.v_cache == nullptr || p->tok0.q == nullptr ||
+      uint64_t(p->tok0.pos) + p->n > p->tok0.max_ctx)
+    return MISO_ERR_INVALID;
+  if (p->n == 0)
+    return MISO_OK;
+  k::attn_prep_batch_kernel<256><<<p->n * 18, 256, 0, as_stream(stream)>>>(
+      *reinterpret_cast<const k::AttnPrepBatchParams*>(p));
+  return launch_status();
+}
+
+int miso_attn_split(const miso_attn_split_params* p, void* stream) {
+  if (p == nullptr || p->q == nullptr || p->k_cache == nullptr || p->v_cache == nullptr ||
+      p->part_m == nullptr || p->part_l == nullptr || p->part_o == nullptr || p->n_splits == 0 ||
+      p->len == 0 || p->len > p->max_ctx || p->n_splits > 65535 || !aligned16(p->k_cache) ||
+      !aligned16(p->v_cache) || !aligned16(p->part_o))
+    return MISO_ERR_INVALID;
+  k::attn_split_kernel<256><<<dim3(p->n_splits, 2), 256, 0, as_stream(stream)>>>(
+      *reinterpret_cast<const k::AttnSplitParams*>(p));
+  return launch_status();
+}
+
+int miso_attn_combine(const miso_attn_combine_params* p, void* stream) {
+  if (p == nullptr || p->part_m == nullptr || p->part_l == nullptr || p->part_o == nullptr ||
+      p->qg == nullptr || p->core == nullptr || p->n_splits == 0)
+    return MISO_ERR_INVALID;
+  k::attn_combine_kernel<64, true, 4><<<64, 64, 0, as_stream(stream)>>>(
+      *reinterpret_cast<const k::AttnCombineParams*>(p));
+  return launch_status();
+}
+
+int miso_attn_prefill(const miso_attn_prefill_params* p, void* stream) {
+  if (p == nullptr || p->q == nullptr || p->qg == nullptr || p->k_cache == nullptr ||
+      p->v_cache == nullptr || p->core == nullptr || uint64_t(p->pos0) + p->n > p->max_ctx ||
+      !aligned16(p->v_cache))
+    return MISO_ERR_INVALID;
+  if (p->n == 0)
+    return MISO_OK;
+  k::attn_prefill_kernel<256><<<k::attn_prefill_items(p->n), 256, 0, as_stream(stream)>>>(
+      *reinterpret_cast<const k::AttnPrefillParams*>(p));
+  return launch_status();
+}
+
+int miso_deltanet_step(const miso_deltanet_step_params* p, void* stream) {
+  if (p == nullptr || p->qkv == nullptr || p->z == nullptr || p->a == nullptr ||
+      p->b == nullptr || p->conv_w == nullptr || p->conv_in == nullptr ||
+      p->conv_out == nullptr || p->ssm_a == nullptr || p->dt_bias == nullptr ||
+      p->norm_w == nullptr || p->state == nullptr || p->out == nullptr || !aligned16(p->state))
+    return MISO_ERR_INVALID;
+  k::deltanet_step_kernel<256><<<32, 256, 0, as_stream(stream)>>>(
+      *reinterpret_cast<const k::DeltaNetStepParams*>(p));
+  return launch_status();
+}
+
+int miso_deltanet_seq(const miso_deltanet_seq_params* p, void* stream) {
+  if (p == nullptr || p->qkv == nullptr || p->z == nullptr || p->a == nullptr ||
+      p->b == nullptr || p->conv_w == nullptr || p->conv_in == nullptr ||
+      p->conv_out == nullptr || p->ssm_a == nullptr || p->dt_bias == nullptr ||
+      p->norm_w == nullptr || p->state == nullptr || p->out == nullptr || !aligned16(p->state))
+    return MISO_ERR_INVALID;
+  k::deltanet_seq_kernel<256><<<32, 256, 0, as_stream(stream)>>>(
+      *reinterpret_cast<const k::DeltaNetSeqParams*>(p));
+  return launch_status();
+}
+
+int miso_deltanet_conv(const miso_deltanet_conv_params* p, void* stream) {
+  if (p == nullptr || p->qkv == nullptr || p->conv_w == nullptr || p->conv_in == nullptr ||
+      p->conv_out == nullptr || p->q == nullptr || p->k == nullptr || p->v == nullptr)
+    return MISO_ERR_INVALID;
+  k::deltanet_conv_kernel<<<32, 256, 0, as_stream(stream)>>>(
+      *reinterpret_cast<const k::DeltaNetConvParams*>(p));
+  return launch_status();
+}
+
+int miso_deltanet_norm(const miso_deltanet_conv_params* p, void* stream) {
+  if (p == nullptr || p->q == nullptr || p->k == nullptr || p->a == nullptr || p->b == nullptr ||
+      p->ssm_a == nullptr || p->dt_bias == nullptr || p->beta == nullptr ||
+      p->log_a == nullptr || !aligned16(p->q) || !aligned16(p->k))
+    return MISO_ERR_INVALID;
+  k::deltanet_norm_kernel<<<64, 256, 0, as_stream(stream)>>>(
+      *reinterpret_cast<const k::DeltaNetConvParams*>(p));
+  return launch_status();
+}
+
+int miso_deltanet_chunk(const miso_deltanet_chunk_params* p, void* stream) {
+  if (p == nullptr || p->q == nullptr || p->k == nullptr || p->v == nullptr ||
+      p->beta == nullptr || p->log_a == nullptr || p->z == nullptr || p->norm_w == nullptr ||
+      p->state == nullptr || p->out == nullptr || p->sk == nullptr || p->sq == nullptr ||
+      !aligned16(p->q) || !aligned16(p->k) || !aligned16(p->sq) || !aligned16(p->z) ||
+      !aligned16(p->out))
+    return MISO_ERR_INVALID;
+  k::deltanet_chunk_kernel<256><<<32, 256, 0, as_stream(stream)>>>(
+      *reinterpret_cast<const k::DeltaNetChunkParams*>(p));
+  return launch_status();
+}
+
+// ---- fast family ----------------------------------------------------------------------------
+
+size_t miso_attn_decode_scratch_bytes(unsigned batch) {
+  DeviceInfo* d = nullptr;
+  if (device_info(&d) != MISO_OK)
+    return 0;
+  return decode_counter_bytes(batch) +
+         size_t(2) * d->sms * miso::fast::decode::kPartFloats * sizeof(float);
+}
+
+int miso_attn_decode(const miso_attn_decode_params* p, void* scratch, size_t scratch_bytes,
+                     void* stream) {
+  namespace dec = miso::fast::decode;
+  if (p == nullptr || p->q == nullptr || p->qg == nullptr || p->k_pool == nullptr ||
+      p->v_pool == nullptr || p->kv_row == nullptr || p->lens == nullptr || p->core == nullptr ||
+      p->batch == 0 || p->batch > unsigned(dec::kMaxBatch) || p->pool_rows == 0 ||
+      p->pool_rows >= (uint64_t(1) << 31) || !aligned16(p->k_pool) || !aligned16(p->v_pool) ||
+      (reinterpret_cast<uintptr_t>(p->q) & 7u) != 0 || scratch == nullptr ||
+      (reinterpret_cast<uintptr_t>(scratch) & 255u) != 0)
+    return MISO_ERR_INVALID;
+  DeviceInfo* d = nullptr;
+  int st = device_info(&d);
+  if (st != MISO_OK)
+    return st;
+  if ((st = tensor_map_encoder()) != MISO_OK)
+    return st;
+  const size_t need = decode_counter_bytes(p->batch) +
+                      size_t(2) * d->sms * dec::kPartFloats * sizeof(float);
+  if (scratch_bytes < need)
+    return MISO_ERR_SCRATCH;
+  CUtensorMap kmap, vmap;
+  if ((st = kv_pool_map(&kmap, p->k_pool, p->pool_rows)) != MISO_OK ||
+      (st = kv_pool_map(&vmap, p->v_pool, p->pool_rows)) != MISO_OK)
+    return st;
+  dec::Args a;
+  a.q = p->q;
+  a.qg = p->qg;
+  a.kv_row = p->kv_row;
+  a.lens = p->lens;
+  a.core = p->core;
+  a.counters = static_cast<int*>(scratch);
+  a.parts = reinterpret_cast<float*>(static_cast<char*>(scratch) + decode_counter_bytes(p->batch));
+  a.batch = p->batch;
+  a.qg_stride = p->qg_stride;
+  dec::decode_kernel<<<d->sms, dec::kThreads, dec::kSmemBytes, as_stream(stream)>>>(kmap, vmap,
+                                                                                    a);
+  return launch_status();
+}
+
+int miso_attn_prep_batched(const miso_attn_prep_batched_params* p, void* stream) {
+  if (p == nullptr || p->qg == nullptr || p->k == nullptr || p->v == nullptr ||
+      p->q_norm == nullptr || p->k_norm == nullptr || p->inv_freq == nullptr ||
+      p->k_pool == nullptr || p->v_pool == nullptr || p->kv_row == nullptr ||
+      p->lens == nullptr || p->q == nullptr || p->batch == 0 || p->batch > 65535)
+    return MISO_ERR_INVALID;
+  miso::fast::prep::Args a;
+  a.qg = p->qg;
+  a.k = p->k;
+  a.v = p->v;
+  a.q_norm = p->q_norm;
+  a.k_norm = p->k_norm;
+  a.inv_freq = p->inv_freq;
+  a.k_pool = reinterpret_cast<__half*>(p->k_pool);
+  a.v_pool = reinterpret_cast<__half*>(p->v_pool);
+  a.kv_row = p->kv_row;
+  a.lens = p->lens;
+  a.q = p->q;
+  a.batch = p->batch;
+  a.proj_stride = p->proj_stride;
+  a.eps = p->eps;
+  miso::fast::prep::prep_batched_kernel<<<p->batch, 256, 0, as_stream(stream)>>>(a);
+  return launch_status();
+}
+
+}  // extern "C"

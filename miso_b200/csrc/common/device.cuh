@@ -1,0 +1,192 @@
+#pragma once
+
+// sm_100a device building blocks shared by the fast kernels: shared-memory addressing, mbarriers
+// with bounded waits, TMA tile loads, ldmatrix / movmatrix and the m16n8k16 f16 MMA.
+//
+// Every wait on an mbarrier is bounded by wall-clock time (%globaltimer). When a wait gives up, the
+// kernel records MISO_STATUS_TIMEOUT in the library's device status word and the caller returns
+// instead of spinning forever; the host reads the word with miso_device_status().
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace miso::dev {
+
+// Device status word codes (also in include/miso_cuda.h as MISO_STATUS_*).
+constexpr int kStatusOk = 0;
+constexpr int kStatusTimeout = 1;
+
+// Bound on any single mbarrier wait: 2 s of wall clock. Legitimate waits here are microseconds.
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+
+// Device status word of this library (one per device per loaded copy of the library).
+__device__ int g_status = 0;
+
+__device__ __forceinline__ void set_status(int code) { atomicCAS(&g_status, kStatusOk, code); }
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ---- mbarrier -------------------------------------------------------------------------------
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+// Makes initialised barriers visible to the async proxy (TMA) before first use.
+__device__ __forceinline__ void mbar_init_fence() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(bar)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
+          bar),
+      "r"(bytes)
+      : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Waits for the phase with the given parity to complete. Returns false (and records a timeout in
+// the status word) if it has not completed within kWaitLimitNs.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity))
+    return true;
+  const unsigned long long t0 = globaltimer();
+  for (unsigned i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity))
+      return true;
+    if ((i & 255u) == 0 && globaltimer() - t0 > kWaitLimitNs) {
+      set_status(kStatusTimeout);
+      return false;
+    }
+  }
+}
+
+// Orders this thread's generic-proxy shared-memory writes before later async-proxy (TMA) writes.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ---- TMA --------------------------------------------------------------------------------------
+
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// 2-D tiled load of one box into shared memory; completion is signalled on `bar` (complete_tx).
+// x is the innermost coordinate in elements; x * element size must be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+// Same with an L2 eviction-priority policy (e.g. evict-first for data streamed exactly once).
+__device__ __forceinline__ void tma_load_2d_hint(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                                 uint32_t bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// Byte offset of the 16-byte chunk `chunk` (0..7) of row `row` inside a box written by TMA with
+// CU_TENSOR_MAP_SWIZZLE_128B and 128-byte rows (box base aligned to 1024 bytes).
+__device__ __forceinline__ uint32_t swz128(uint32_t row, uint32_t chunk) {
+  return row * 128u + (((chunk ^ row) & 7u) << 4);
+}
+
+// ---- warp-level tensor-core fragments -------------------------------------------------------
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr)
+               : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                          uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr)
+               : "memory");
+}
+
+// Transpose of an 8x8 b16 matrix held in the standard fragment layout (lane i: row i/4,
+// columns 2(i%4), 2(i%4)+1).
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t a) {
+  uint32_t d;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
+  return d;
+}
+
+// D = A(16x16, row) * B(16x8, col) + D, f16 inputs, f32 accumulate.
+__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                        uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+      "{%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float lo_elem, float hi_elem) {
+  const __half2 h = __floats2half2_rn(lo_elem, hi_elem);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Two-term fp16 split of an fp32 pair: hi = fp16(x), lo = fp16(x - hi). hi + lo carries ~22
+// significant bits, so products against exact fp16 operands keep fp32-level accuracy.
+__device__ __forceinline__ void split_half2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  const __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
+  const __half l0 = __float2half_rn(x0 - __half2float(h0));
+  const __half l1 = __float2half_rn(x1 - __half2float(h1));
+  const __half2 H = __halves2half2(h0, h1), L = __halves2half2(l0, l1);
+  hi = *reinterpret_cast<const uint32_t*>(&H);
+  lo = *reinterpret_cast<const uint32_t*>(&L);
+}
+
+__device__ __forceinline__ void named_bar_sync(unsigned id, unsigned threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+}  // namespace miso::dev

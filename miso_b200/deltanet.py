@@ -1,0 +1,82 @@
+"""Host side of the Gated DeltaNet hot path over torch device tensors.
+
+Mirrors the kernel part of the reference engine's DeltaNet mixer (src/engine/deltanet.hip
+:56-118): DeltaNetState with the double-buffered conv history and the fp32 [32][128][128] state
+(src/engine/deltanet.hpp:24-33), decode = one step kernel then a parity flip, prefill = the fused
+n-token recurrence then a parity flip. The chunked form (conv -> norm -> chunk) is exposed as in
+the reference's test harness (tests/test_deltanet_chunk.hip:76-88).
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import _capi as capi
+from .attention import _ptr, _stream
+
+K_HEADS, V_HEADS, DIM, CHUNK = 16, 32, 128, 64
+CHANNELS = 2 * K_HEADS * DIM + V_HEADS * DIM  # 8192
+PROJ = 12352  # DeltaNetScratch::kProj: [qkv 8192 | z 4096 | a 32 | b 32]
+
+
+class DeltaNetState:
+    def __init__(self, device="cuda"):
+        self.conv = [torch.zeros((CHANNELS, 3), dtype=torch.float32, device=device)
+                     for _ in range(2)]
+        self.s = torch.zeros((V_HEADS, DIM, DIM), dtype=torch.float32, device=device)
+        self.parity = 0
+
+    def reset(self):
+        for c in self.conv:
+            c.zero_()
+        self.s.zero_()
+        self.parity = 0
+
+
+def step(p: capi.DeltaNetStepParams, stream=None) -> None:
+    capi.check("miso_deltanet_step", capi.load().miso_deltanet_step(C.byref(p), _stream(stream)))
+
+
+def seq(p: capi.DeltaNetSeqParams, stream=None) -> None:
+    capi.check("miso_deltanet_seq", capi.load().miso_deltanet_seq(C.byref(p), _stream(stream)))
+
+
+def conv(p: capi.DeltaNetConvParams, stream=None) -> None:
+    capi.check("miso_deltanet_conv", capi.load().miso_deltanet_conv(C.byref(p), _stream(stream)))
+
+
+def norm(p: capi.DeltaNetConvParams, stream=None) -> None:
+    capi.check("miso_deltanet_norm", capi.load().miso_deltanet_norm(C.byref(p), _stream(stream)))
+
+
+def chunk(p: capi.DeltaNetChunkParams, stream=None) -> None:
+    capi.check("miso_deltanet_chunk",
+               capi.load().miso_deltanet_chunk(C.byref(p), _stream(stream)))
+
+
+def deltanet_decode_core(st: DeltaNetState, proj: torch.Tensor, conv_w, ssm_a, dt_bias, norm_w,
+                         out: torch.Tensor, eps: float, stream=None) -> torch.Tensor:
+    """One token from its [12352] projection row (src/engine/deltanet.hip:66-81)."""
+    base = proj.data_ptr()
+    p = capi.DeltaNetStepParams(base, base + 8192 * 4, base + 12288 * 4, base + 12320 * 4,
+                                _ptr(conv_w), _ptr(st.conv[st.parity]),
+                                _ptr(st.conv[1 - st.parity]), _ptr(ssm_a), _ptr(dt_bias),
+                                _ptr(norm_w), _ptr(st.s), _ptr(out), eps)
+    step(p, stream)
+    st.parity = 1 - st.parity
+    return out
+
+
+def deltanet_prefill_core(st: DeltaNetState, proj: torch.Tensor, n: int, conv_w, ssm_a, dt_bias,
+                          norm_w, out: torch.Tensor, eps: float, stream=None) -> torch.Tensor:
+    """n tokens from a [n][12352] projection buffer (src/engine/deltanet.hip:97-115)."""
+    base = proj.data_ptr()
+    z = base + 8192 * 4
+    p = capi.DeltaNetSeqParams(base, z, z + 4096 * 4, z + 4128 * 4, _ptr(conv_w),
+                               _ptr(st.conv[st.parity]), _ptr(st.conv[1 - st.parity]),
+                               _ptr(ssm_a), _ptr(dt_bias), _ptr(norm_w), _ptr(st.s), _ptr(out),
+                               n, eps, PROJ, PROJ)
+    seq(p, stream)
+    st.parity = 1 - st.parity
+    return out

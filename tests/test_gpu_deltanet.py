@@ -1,0 +1,172 @@
+"""GPU parity of the Gated DeltaNet kernels (through the C ABI) against the CPU oracle, plus the
+reference's own GPU-vs-GPU pins: the fused n-token recurrence equals n single steps bit for bit
+(kernels/deltanet_step.hpp:142-145), and the chunked path (conv -> norm -> chunk) matches the
+recurrence with the conv history bit-equal and outputs / state within 1e-4
+(tests/test_deltanet_chunk.hip:24-109, same parameterisation)."""
+import numpy as np
+import pytest
+import torch
+
+from miso_b200 import _capi as capi
+from miso_b200 import deltanet as DN
+import inputs as I
+import oracle
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda")
+
+
+def T(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+
+
+def ptr(t):
+    return t.data_ptr()
+
+
+def rel(got, ref):
+    got, ref = np.asarray(got, np.float64), np.asarray(ref, np.float64)
+    den = np.sqrt((ref ** 2).sum())
+    return float(np.sqrt(((got - ref) ** 2).sum()) / den) if den > 0 else 0.0
+
+
+def chunk_test_inputs(n):
+    """tests/test_deltanet_chunk.hip:24-55: N(0, 0.5) inputs, ssm_a = -0.05 (h + 1),
+    dt = 0.1 h, norm_w = 1 + 0.01 (i - 64), z / a / b packed at stride 4160."""
+    rng = np.random.RandomState(n + 3)
+    nd = lambda *s: (0.5 * rng.standard_normal(s)).astype(np.float32)  # noqa: E731
+    qkv, z, a, b = nd(n, 8192), nd(n, 4096), nd(n, 32), nd(n, 32)
+    conv_w, conv_in, state = nd(8192, 4), nd(8192, 3), nd(32, 128, 128)
+    ssm_a = (-0.05 * (np.arange(32) + 1)).astype(np.float32)
+    dt = (0.1 * np.arange(32)).astype(np.float32)
+    norm_w = (1.0 + 0.01 * (np.arange(128) - 64)).astype(np.float32)
+    zab = np.zeros((n, 4160), np.float32)
+    zab[:, :4096], zab[:, 4096:4128], zab[:, 4128:] = z, a, b
+    return dict(n=n, qkv=qkv, z=z, a=a, b=b, conv_w=conv_w, conv_in=conv_in, state=state,
+                ssm_a=ssm_a, dt=dt, norm_w=norm_w, zab=zab)
+
+
+def run_seq(x, state=None, conv_in=None):
+    n = x["n"]
+    d = {k: T(x[k]) for k in ("qkv", "zab", "conv_w", "ssm_a", "dt", "norm_w")}
+    st = T(x["state"] if state is None else state)
+    ci = T(x["conv_in"] if conv_in is None else conv_in)
+    co = torch.empty_like(ci)
+    out = torch.empty((n, 4096), device=DEV)
+    zb = ptr(d["zab"])
+    DN.seq(capi.DeltaNetSeqParams(ptr(d["qkv"]), zb, zb + 4096 * 4, zb + 4128 * 4,
+                                  ptr(d["conv_w"]), ptr(ci), ptr(co), ptr(d["ssm_a"]),
+                                  ptr(d["dt"]), ptr(d["norm_w"]), ptr(st), ptr(out), n, 1e-6,
+                                  4160, 8192))
+    torch.cuda.synchronize()
+    return out.cpu().numpy(), st.cpu().numpy(), co.cpu().numpy()
+
+
+def test_step_matches_oracle():
+    x = chunk_test_inputs(3)
+    d = {k: T(x[k]) for k in ("conv_w", "ssm_a", "dt", "norm_w")}
+    conv = [T(x["conv_in"]), torch.empty((8192, 3), device=DEV)]
+    st = T(x["state"])
+    conv64 = x["conv_in"].astype(np.float64)[None].copy()
+    st64 = x["state"].astype(np.float64)[None].copy()
+    for t in range(3):
+        qkv, z, a, b = (T(x[k][t]) for k in ("qkv", "z", "a", "b"))
+        out = torch.empty(4096, device=DEV)
+        DN.step(capi.DeltaNetStepParams(ptr(qkv), ptr(z), ptr(a), ptr(b), ptr(d["conv_w"]),
+                                        ptr(conv[t % 2]), ptr(conv[1 - t % 2]), ptr(d["ssm_a"]),
+                                        ptr(d["dt"]), ptr(d["norm_w"]), ptr(st), ptr(out), 1e-6))
+        torch.cuda.synchronize()
+        ref = oracle.deltanet_step(x["qkv"][t][None], x["z"][t][None], x["a"][t][None],
+                                   x["b"][t][None], x["conv_w"], conv64, x["ssm_a"], x["dt"],
+                                   x["norm_w"], st64, 1e-6)
+        assert rel(out.cpu().numpy(), ref[0]) < 1e-5
+        assert np.array_equal(conv[1 - t % 2].cpu().numpy().astype(np.float64), conv64[0])
+    assert rel(st.cpu().numpy(), st64[0]) < 1e-5
+
+
+def test_sequence_equals_steps_bitwise():
+    x = chunk_test_inputs(7)
+    out_seq, st_seq, co_seq = run_seq(x)
+    d = {k: T(x[k]) for k in ("conv_w", "ssm_a", "dt", "norm_w")}
+    conv = [T(x["conv_in"]), torch.empty((8192, 3), device=DEV)]
+    st = T(x["state"])
+    outs = []
+    for t in range(7):
+        qkv, z, a, b = (T(x[k][t]) for k in ("qkv", "z", "a", "b"))
+        out = torch.empty(4096, device=DEV)
+        DN.step(capi.DeltaNetStepParams(ptr(qkv), ptr(z), ptr(a), ptr(b), ptr(d["conv_w"]),
+                                        ptr(conv[t % 2]), ptr(conv[1 - t % 2]), ptr(d["ssm_a"]),
+                                        ptr(d["dt"]), ptr(d["norm_w"]), ptr(st), ptr(out), 1e-6))
+        outs.append(out.cpu().numpy())
+    torch.cuda.synchronize()
+    assert np.array_equal(np.stack(outs).view(np.uint32), out_seq.view(np.uint32))
+    assert np.array_equal(st.cpu().numpy().view(np.uint32), st_seq.view(np.uint32))
+    assert np.array_equal(conv[1].cpu().numpy(), co_seq)
+
+
+def test_sequence_matches_transformers_golden_and_oracle():
+    x = I.deltanet_inputs()
+    n = x["n"]
+    zab = np.zeros((n, 4160), np.float32)
+    zab[:, :4096], zab[:, 4096:4128], zab[:, 4128:] = x["z"], x["a"], x["b"]
+    y = dict(n=n, qkv=x["qkv"], zab=zab, conv_w=x["conv_w"], conv_in=x["conv_in"],
+             state=x["state"], ssm_a=x["ssm_a"], dt=x["dt_bias"], norm_w=x["norm_w"])
+    out, st, _ = run_seq(y)
+    gold = np.load(I.__file__.replace("inputs.py", "golden.npz"))
+    out3 = out.reshape(n, 32, 128)
+    assert rel(out3[:, list(I.DN_HEADS)], gold["dn_out_rec"]) < 1e-4
+    assert rel(st[I.DN_STATE_HEAD], gold["dn_state_rec"]) < 1e-4
+    conv = x["conv_in"].astype(np.float64).copy()
+    s64 = x["state"].astype(np.float64).copy()
+    ref = oracle.deltanet_seq(n, x["qkv"], 8192, zab, 4160, x["conv_w"], conv, x["ssm_a"],
+                              x["dt_bias"], x["norm_w"], s64, 1e-6)
+    assert rel(out, ref) < 1e-4
+    assert rel(st, s64) < 1e-4
+
+
+def run_chunk_path(x):
+    n = x["n"]
+    d = {k: T(x[k]) for k in ("qkv", "a", "b", "conv_w", "conv_in", "ssm_a", "dt", "z",
+                              "norm_w")}
+    st = T(x["state"])
+    co = torch.empty((8192, 3), device=DEV)
+    q = torch.empty((n, 16, 128), device=DEV)
+    k = torch.empty((n, 16, 128), device=DEV)
+    v = torch.empty((n, 32, 128), device=DEV)
+    beta = torch.empty((n, 32), device=DEV)
+    log_a = torch.empty((n, 32), device=DEV)
+    sk = torch.empty((32, 64, 128), device=DEV)
+    sq = torch.empty((32, 64, 128), device=DEV)
+    out = torch.empty((n, 4096), device=DEV)
+    cp = capi.DeltaNetConvParams(ptr(d["qkv"]), ptr(d["a"]), ptr(d["b"]), ptr(d["conv_w"]),
+                                 ptr(d["conv_in"]), ptr(co), ptr(d["ssm_a"]), ptr(d["dt"]),
+                                 ptr(q), ptr(k), ptr(v), ptr(beta), ptr(log_a), n)
+    DN.conv(cp)
+    DN.norm(cp)
+    DN.chunk(capi.DeltaNetChunkParams(ptr(q), ptr(k), ptr(v), ptr(beta), ptr(log_a), ptr(d["z"]),
+                                      ptr(d["norm_w"]), ptr(st), ptr(out), ptr(sk), ptr(sq), n,
+                                      1e-6))
+    torch.cuda.synchronize()
+    return out.cpu().numpy(), st.cpu().numpy(), co.cpu().numpy()
+
+
+@pytest.mark.parametrize("n", [1, 7, 64, 65, 128, 200])
+def test_chunked_path_matches_recurrence(n):
+    x = chunk_test_inputs(n)
+    o_seq, s_seq, c_seq = run_seq(x)
+    o_ch, s_ch, c_ch = run_chunk_path(x)
+    assert np.array_equal(c_ch, c_seq)
+    assert rel(o_ch, o_seq) <= 1e-4
+    assert rel(s_ch, s_seq) <= 1e-4
+
+
+def test_chunked_path_matches_oracle():
+    x = chunk_test_inputs(130)
+    o_ch, s_ch, _ = run_chunk_path(x)
+    conv = x["conv_in"].astype(np.float64).copy()
+    q, k, v, beta, log_a = oracle.deltanet_prepare(130, x["qkv"], x["a"], x["b"], x["conv_w"],
+                                                   conv, x["ssm_a"], x["dt"])
+    s64 = x["state"].astype(np.float64).copy()
+    ref = oracle.deltanet_chunk(130, q, k, v, beta, log_a, x["z"], x["norm_w"], s64, 1e-6)
+    assert rel(o_ch, ref) <= 1e-4
+    assert rel(s_ch, s64) <= 1e-4
