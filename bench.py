@@ -349,15 +349,20 @@ def run_miso(args) -> None:
 
 
 def main():
+    global BATCH
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["miso", "reference"], default="miso")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=BATCH,
+                    help="sequences per GPU (default 32, the BASELINE config; smaller only for "
+                         "profiling captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    BATCH = args.batch
     if args.impl == "reference":
         run_reference(args)
     else:

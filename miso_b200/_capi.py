@@ -121,7 +121,7 @@ def load(path: str | None = None) -> C.CDLL:
     path = path or _build.LIB
     if not os.path.exists(path):
         raise ImportError(
-            f"miso_b200: CUDA library not built ({path}); run `python -m miso_b200.build`")
+            f"miso_b200: CUDA library not built ({path}); run `python miso_b200/build.py`")
     lib = C.CDLL(path)
     for name, (res, args) in SIGNATURES.items():
         fn = getattr(lib, name)

@@ -179,7 +179,10 @@ int miso_device_status(int reset, int* status) {
 int miso_attn_prep(const miso_attn_prep_params* p, void* stream) {
   if (p == nullptr || p->qg == nullptr || p->k == nullptr || p->v == nullptr ||
       p->q_norm == nullptr || p->k_norm == nullptr || p->inv_freq == nullptr ||
-      p->k_cache == nullptr || p->v_cache == nullptr || p->q == nullptr || p->pos >= p->max_ctx)
+      p->k_cache == nullptr || p->v_cache == nullptr || p->q == nullptr || p->pos >= p->max_ctx ||
+      !aligned16(p->qg) || !aligned16(p->k) || !aligned16(p->v) || !aligned16(p->q_norm) ||
+      !aligned16(p->k_norm) || !aligned16(p->q) || !aligned16(p->k_cache) ||
+      !aligned16(p->v_cache))
     return MISO_ERR_INVALID;
   k::attn_prep_kernel<256><<<18, 256, 0, as_stream(stream)>>>(
       *reinterpret_cast<const k::AttnPrepParams*>(p));
@@ -190,7 +193,10 @@ int miso_attn_prep_batch(const miso_attn_prep_batch_params* p, void* stream) {
   if (p == nullptr || p->tok0.qg == nullptr || p->tok0.k == nullptr || p->tok0.v == nullptr ||
       p->tok0.q_norm == nullptr || p->tok0.k_norm == nullptr || p->tok0.inv_freq == nullptr ||
       p->tok0.k_cache == nullptr || p->tok0.v_cache == nullptr || p->tok0.q == nullptr ||
-      uint64_t(p->tok0.pos) + p->n > p->tok0.max_ctx)
+      uint64_t(p->tok0.pos) + p->n > p->tok0.max_ctx || p->proj_stride % 4 != 0 ||
+      !aligned16(p->tok0.qg) || !aligned16(p->tok0.k) || !aligned16(p->tok0.v) ||
+      !aligned16(p->tok0.q_norm) || !aligned16(p->tok0.k_norm) || !aligned16(p->tok0.q) ||
+      !aligned16(p->tok0.k_cache) || !aligned16(p->tok0.v_cache))
     return MISO_ERR_INVALID;
   if (p->n == 0)
     return MISO_OK;
@@ -337,7 +343,10 @@ int miso_attn_prep_batched(const miso_attn_prep_batched_params* p, void* stream)
   if (p == nullptr || p->qg == nullptr || p->k == nullptr || p->v == nullptr ||
       p->q_norm == nullptr || p->k_norm == nullptr || p->inv_freq == nullptr ||
       p->k_pool == nullptr || p->v_pool == nullptr || p->kv_row == nullptr ||
-      p->lens == nullptr || p->q == nullptr || p->batch == 0 || p->batch > 65535)
+      p->lens == nullptr || p->q == nullptr || p->batch == 0 || p->batch > 65535 ||
+      p->proj_stride % 4 != 0 || !aligned16(p->qg) || !aligned16(p->k) || !aligned16(p->v) ||
+      !aligned16(p->q_norm) || !aligned16(p->k_norm) || !aligned16(p->q) ||
+      !aligned16(p->k_pool) || !aligned16(p->v_pool))
     return MISO_ERR_INVALID;
   miso::fast::prep::Args a;
   a.qg = p->qg;
@@ -354,7 +363,8 @@ int miso_attn_prep_batched(const miso_attn_prep_batched_params* p, void* stream)
   a.batch = p->batch;
   a.proj_stride = p->proj_stride;
   a.eps = p->eps;
-  miso::fast::prep::prep_batched_kernel<<<p->batch, 256, 0, as_stream(stream)>>>(a);
+  miso::fast::prep::prep_batched_kernel<<<p->batch, miso::fast::prep::kThreads, 0,
+                                           as_stream(stream)>>>(a);
   return launch_status();
 }
 

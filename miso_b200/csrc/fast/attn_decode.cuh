@@ -305,8 +305,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       __threadfence();
       dev::named_bar_sync(1, kConsumers);
       if (tid == 0) {
+        // CTAs between the segment's first and last owner may have empty ranges (T < P).
+        int parts = 0;
+        for (unsigned cc = c_first; cc <= c_last; ++cc)
+          parts += range_begin(cc, T, P) < range_begin(cc + 1, T, P);
         const int prev = atomicAdd(&a.counters[seg], 1);
-        sm.is_last = prev == static_cast<int>(c_last - c_first);
+        sm.is_last = prev == parts - 1;
       }
       dev::named_bar_sync(1, kConsumers);
       if (sm.is_last) {
@@ -317,12 +321,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           const unsigned h = i / kDim, d = i % kDim;
           float M = kNegInf;
           for (unsigned cc = c_first; cc <= c_last; ++cc) {
+            if (range_begin(cc, T, P) == range_begin(cc + 1, T, P))
+              continue;  // empty range: no partial
             const unsigned sl = (cc > c_first || seg_at_cfirst_start) ? 0 : 1;
             const float* pp = a.parts + (size_t(2) * cc + sl) * kPartFloats;
             M = fmaxf(M, __ldcg(pp + h));
           }
           float L = 0.0f, ov = 0.0f;
           for (unsigned cc = c_first; cc <= c_last; ++cc) {
+            if (range_begin(cc, T, P) == range_begin(cc + 1, T, P))
+              continue;
             const unsigned sl = (cc > c_first || seg_at_cfirst_start) ? 0 : 1;
             const float* pp = a.parts + (size_t(2) * cc + sl) * kPartFloats;
             const float mc = __ldcg(pp + h);

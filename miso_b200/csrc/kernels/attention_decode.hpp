@@ -51,57 +51,85 @@ struct AttnPrepBatchParams {
 
 namespace attn_detail {
 
-// One row of 256 (a query head or a key head) on a 256-thread block: RMSNorm with `weight`,
-// NEOX rotation of dims [0, 64) at position `pos`, then either an fp32 store (out_f32) or an fp16
-// cache store (out_f16, plus the matching value row v_src -> v_dst). Ends with a barrier so the
-// shared row can be reused.
-template <int kBlock>
-__device__ __forceinline__ void prep_row(const float* src, const float* weight,
-                                         const float* inv_freq, unsigned pos, float eps,
-                                         float* out_f32, attn::half_t* out_f16, const float* v_src,
-                                         attn::half_t* v_dst) {
+// One row of 256 (a query head or a key head) on one warp, lane l owning dims [8l, 8l + 8):
+// RMSNorm with `weight`, NEOX rotation of dims [0, 64) at position `pos` (dim d < 32 pairs with
+// d + 32, i.e. lane l < 4 with lane l + 4), then either an fp32 store (out_f32) or an fp16 cache
+// store (out_f16, plus the matching value row v_src -> v_dst). Warp-synchronous, no shared memory,
+// so the drop-in and batched prep kernels produce identical bits.
+__device__ __forceinline__ void prep_row_warp(const float* src, const float* weight,
+                                              const float* inv_freq, unsigned pos, float eps,
+                                              float* out_f32, attn::half_t* out_f16,
+                                              const float* v_src, attn::half_t* v_dst) {
   using namespace attn;
-  static_assert(kBlock == kDim, "one thread per dimension");
-  __shared__ float row[kDim];
-  __shared__ float red[kBlock / kWave];
-  const unsigned d = threadIdx.x;
-  const float x = src[d];
-  const float inv_rms = rsqrtf(block_sum<kBlock>(x * x, red) / kDim + eps);
-  float y = x * inv_rms * weight[d];
-  row[d] = y;
-  __syncthreads();
-  if (d < kRopeDim) {
+  const unsigned lane = threadIdx.x % kWave;
+  float y[8], w[8];
+  const float4* s4 = reinterpret_cast<const float4*>(src) + 2 * lane;
+  const float4* w4 = reinterpret_cast<const float4*>(weight) + 2 * lane;
+  {
+    const float4 a = s4[0], b = s4[1], c = w4[0], d = w4[1];
+    y[0] = a.x, y[1] = a.y, y[2] = a.z, y[3] = a.w, y[4] = b.x, y[5] = b.y, y[6] = b.z, y[7] = b.w;
+    w[0] = c.x, w[1] = c.y, w[2] = c.z, w[3] = c.w, w[4] = d.x, w[5] = d.y, w[6] = d.z, w[7] = d.w;
+  }
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    ss += y[i] * y[i];
+  const float inv_rms = rsqrtf(wave_sum(ss) / kDim + eps);
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    y[i] = y[i] * inv_rms * w[i];
+  float partner[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    partner[i] = __shfl_xor_sync(0xffffffffu, y[i], 4);
+  if (lane < kRopeDim / 8) {
     constexpr unsigned kHalf = kRopeDim / 2;
-    const unsigned i = d % kHalf;
-    float sn, cs;
-    sincosf(static_cast<float>(pos) * inv_freq[i], &sn, &cs);
-    const float lo = row[i], hi = row[i + kHalf];
-    y = d < kHalf ? lo * cs - hi * sn : hi * cs + lo * sn;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const unsigned d = 8 * lane + i;
+      float sn, cs;
+      sincosf(static_cast<float>(pos) * inv_freq[d % kHalf], &sn, &cs);
+      y[i] = d < kHalf ? y[i] * cs - partner[i] * sn : y[i] * cs + partner[i] * sn;
+    }
   }
   if (out_f32 != nullptr) {
-    out_f32[d] = y;
+    float4* o4 = reinterpret_cast<float4*>(out_f32) + 2 * lane;
+    o4[0] = make_float4(y[0], y[1], y[2], y[3]);
+    o4[1] = make_float4(y[4], y[5], y[6], y[7]);
   } else {
-    out_f16[d] = __float2half_rn(y);
-    v_dst[d] = __float2half_rn(v_src[d]);
+    __align__(16) __half h[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      h[i] = __float2half_rn(y[i]);
+    reinterpret_cast<uint4*>(out_f16)[lane] = *reinterpret_cast<const uint4*>(h);
+    const float4* v4 = reinterpret_cast<const float4*>(v_src) + 2 * lane;
+    const float4 a = v4[0], b = v4[1];
+    __align__(16) __half hv[8] = {__float2half_rn(a.x), __float2half_rn(a.y),
+                                  __float2half_rn(a.z), __float2half_rn(a.w),
+                                  __float2half_rn(b.x), __float2half_rn(b.y),
+                                  __float2half_rn(b.z), __float2half_rn(b.w)};
+    reinterpret_cast<uint4*>(v_dst)[lane] = *reinterpret_cast<const uint4*>(hv);
   }
-  __syncthreads();
 }
 
 }  // namespace attn_detail
 
 // Head `head` of 18 (0..15 query heads, 16..17 KV heads): norm, RoPE at p.pos, then store q or
-// append k / v at cache position p.pos.
+// append k / v at cache position p.pos. The first warp of the block does the row.
 template <int kBlock>
 __device__ void attn_prep_head(const AttnPrepParams& p, unsigned head) {
   using namespace attn;
+  static_assert(kBlock % kWave == 0, "whole warps");
+  if (threadIdx.x >= kWave)
+    return;
   if (head < kQHeads) {
-    attn_detail::prep_row<kBlock>(p.qg + head * 2 * kDim, p.q_norm, p.inv_freq, p.pos, p.eps,
-                                  p.q + head * kDim, nullptr, nullptr, nullptr);
+    attn_detail::prep_row_warp(p.qg + head * 2 * kDim, p.q_norm, p.inv_freq, p.pos, p.eps,
+                               p.q + head * kDim, nullptr, nullptr, nullptr);
   } else {
     const unsigned kvh = head - kQHeads;
     const std::size_t at = (std::size_t{kvh} * p.max_ctx + p.pos) * kDim;
-    attn_detail::prep_row<kBlock>(p.k + kvh * kDim, p.k_norm, p.inv_freq, p.pos, p.eps, nullptr,
-                                  p.k_cache + at, p.v + kvh * kDim, p.v_cache + at);
+    attn_detail::prep_row_warp(p.k + kvh * kDim, p.k_norm, p.inv_freq, p.pos, p.eps, nullptr,
+                               p.k_cache + at, p.v + kvh * kDim, p.v_cache + at);
   }
 }
 

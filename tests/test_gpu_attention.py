@@ -221,7 +221,7 @@ def test_fast_decode_equals_drop_in_path_on_a_reference_cache():
     pool.lens.fill_(length)
     fast, _ = run_fast(pool, q[None], qg[None])
     drop, _, _ = run_split_combine(q, qg, k, v, length, max_ctx, 60)
-    assert rel_per_head(fast[0], drop) <= 2e-6
+    assert rel_per_head(fast[0], drop) <= 1e-5  # both within 1e-5 of fp64
 
 
 # ---- prep (tests of the reference: via test_attention / prefill; formulas
