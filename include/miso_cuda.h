@@ -43,7 +43,8 @@ enum {
   MISO_ERR_INVALID = -1,   /* null pointer, size out of range or misaligned buffer */
   MISO_ERR_SCRATCH = -2,   /* scratch buffer smaller than the *_scratch_bytes() figure */
   MISO_ERR_NO_DEVICE = -3, /* no CUDA device, or not an sm_100 device */
-  MISO_ERR_DRIVER = -4     /* a driver entry point (tensor-map encoding) was unavailable */
+  MISO_ERR_DRIVER = -4,    /* a driver entry point (tensor-map encoding) was unavailable */
+  MISO_ERR_LIMIT = -5      /* request exceeds a fixed capacity (miso_attn_decode_noalloc) */
 };
 
 /* Device status word (miso_device_status). */
@@ -237,6 +238,15 @@ typedef struct {
 size_t miso_attn_decode_scratch_bytes(unsigned batch);
 int miso_attn_decode(const miso_attn_decode_params* p, void* scratch, size_t scratch_bytes,
                      void* stream);
+
+/* miso_attn_decode for callers that cannot allocate device memory (no counterpart in the
+ * reference, which is single-sequence and passes caller-owned scratch). Same parameters and
+ * results as miso_attn_decode, without the scratch argument: the scratch is a fixed array inside
+ * the library (2,643,968 bytes, present on every GPU that loads the library until exit). Limits:
+ * batch <= 256 (MISO_ERR_LIMIT beyond). Allocates nothing. The first call on each device looks up
+ * the array's address and should come before any stream capture. All calls on a device share the
+ * array: calls that overlap on the GPU race. */
+int miso_attn_decode_noalloc(const miso_attn_decode_params* p, void* stream);
 
 /* Batched decode prep: attn_prep_kernel (kernels/attention_decode.hpp:41-83) for `batch`
  * sequences, each at its own position pos = lens[b]; appends K/V to the pool rows kv_row[2b+h] +

@@ -94,13 +94,14 @@ SIGNATURES = {
     "miso_deltanet_chunk": (C.c_int, [C.POINTER(DeltaNetChunkParams), _P]),
     "miso_attn_decode_scratch_bytes": (C.c_size_t, [_U]),
     "miso_attn_decode": (C.c_int, [C.POINTER(AttnDecodeParams), _P, C.c_size_t, _P]),
+    "miso_attn_decode_noalloc": (C.c_int, [C.POINTER(AttnDecodeParams), _P]),
     "miso_attn_prep_batched": (C.c_int, [C.POINTER(AttnPrepBatchedParams), _P]),
     "miso_device_status": (C.c_int, [C.c_int, C.POINTER(C.c_int)]),
     "miso_version": (C.c_char_p, []),
 }
 
 ERRORS = {-1: "MISO_ERR_INVALID", -2: "MISO_ERR_SCRATCH", -3: "MISO_ERR_NO_DEVICE",
-          -4: "MISO_ERR_DRIVER"}
+          -4: "MISO_ERR_DRIVER", -5: "MISO_ERR_LIMIT"}
 
 
 class MisoError(RuntimeError):

@@ -369,3 +369,6 @@ int miso_attn_prep_batched(const miso_attn_prep_batched_params* p, void* stream)
 }
 
 }  // extern "C"
+
+// No-allocation variant of miso_attn_decode (its own file, same translation unit).
+#include "decode_noalloc.cu"
