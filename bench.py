@@ -297,6 +297,9 @@ def run_miso(args) -> None:
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
 
+    prefill = None if args.no_prefill else bench_prefill(args, dev, stream, max_over_ranks,
+                                                         barrier, world)
+
     st = ctypes.c_int(-1)
     capi.check("miso_device_status", capi.load().miso_device_status(1, st))
     if st.value != 0:
@@ -344,8 +347,85 @@ def run_miso(args) -> None:
         "gpu_launches": 2 * args.steps,
         "clocks": clk.summary(),
         "cpu_baseline": cpu,
+        "prefill": prefill,
     }
     print(json.dumps(line), flush=True)
+
+
+PREFILL_N = 8192
+
+
+def prefill_flops(n: int, pos0: int = 0) -> float:
+    """Causal QK^T + PV FLOPs of 16 heads x 256 dims: 4 * 16 * 256 * sum_t (pos0 + t + 1)."""
+    return 4.0 * 16 * 256 * (n * pos0 + n * (n + 1) / 2)
+
+
+def bench_prefill(args, dev, stream, max_over_ranks, barrier, world) -> dict:
+    """one 8192-token causal gated prefill per GPU (bf16 inputs, fp16 tensor
+    operands, fp32 softmax / accumulation). Step = prep (norm, RoPE, fp16 KV append) + tcgen05
+    attention; TFLOP/s counts the causal attention FLOPs 8192 n (n + 1)."""
+    import torch
+    from miso_b200 import attention as A
+    from miso_b200 import capi
+
+    n = PREFILL_N
+    g = torch.Generator(device=dev)
+    g.manual_seed(99)
+    proj = torch.randn((n, PROJ), generator=g, device=dev).bfloat16().float()  # bf16 values
+    ones = torch.ones(DIM, device=dev)
+    inv_freq = torch.from_numpy(A.rope_inv_freq()).to(dev)
+    kc = torch.empty((KV_HEADS, n, DIM), dtype=torch.float16, device=dev)
+    vc = torch.empty_like(kc)
+    q16 = torch.empty((n, Q_HEADS, DIM), dtype=torch.float16, device=dev)
+    core = torch.empty((n, Q_HEADS, DIM), device=dev)
+    base = proj.data_ptr()
+    tok0 = capi.AttnPrepParams(base, base + 8192 * 4, base + 8704 * 4, ones.data_ptr(),
+                               ones.data_ptr(), inv_freq.data_ptr(), kc.data_ptr(), vc.data_ptr(),
+                               0, 0, n, EPS)
+    bp = capi.AttnPrepBatchParams(tok0, n, PROJ)
+    tp = capi.AttnPrefillTcParams(q16.data_ptr(), base, kc.data_ptr(), vc.data_ptr(),
+                                  core.data_ptr(), 0, n, n, PROJ)
+    lib = capi.load()
+
+    def step(ev=None):
+        capi.check("prep_f16", lib.miso_attn_prep_batch_f16(ctypes.byref(bp), q16.data_ptr(),
+                                                            stream.cuda_stream))
+        if ev is not None:
+            ev[0].record(stream)
+        capi.check("prefill_tc", lib.miso_attn_prefill_tc(ctypes.byref(tp), stream.cuda_stream))
+        if ev is not None:
+            ev[1].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for i in range(args.steps):
+        step(evs[i])
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    step_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    kern_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in evs) / args.steps)
+    flops = prefill_flops(n)
+    pk = peaks()
+    achieved = flops / (kern_ms * 1e-3) / 1e12
+    return {"metric": "prefill TFLOP/s @8k", "value": world * flops / (step_ms * 1e-3) / 1e12,
+            "unit": "TFLOP/s", "ms_per_step": step_ms, "n_tokens": n,
+            "config": "BASELINE config 3: 1 x 8192 tokens per GPU, causal, 16 Q / 2 KV heads, "
+                      "d 256, RoPE 64 dims theta 1e7, sigmoid gate, bf16 inputs, fp16 tensor "
+                      "operands, fp32 softmax / accumulate; step = prep + attention",
+            "flops_per_step": flops,
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"],
+                         "unit": "TFLOP/s", "frac": achieved / pk["bf16_tflops"],
+                         "traffic": None, "kernel": "prefill_kernel", "kernel_ms": kern_ms,
+                         "peak_source": pk["source"] + " (dense bf16 burst; fp16 equal)"},
+            "gpu_launches": 2 * args.steps}
 
 
 def main():
@@ -356,6 +436,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["miso", "reference"], default="miso")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true",
+                    help="skip the prefill leg (BASELINE config 3) of the JSON line")
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="sequences per GPU (default 32, the BASELINE config; smaller only for "
                          "profiling captures)")

@@ -272,6 +272,28 @@ typedef struct {
 
 int miso_attn_prep_batched(const miso_attn_prep_batched_params* p, void* stream);
 
+/* Causal gated prefill on the tcgen05 tensor cores: the computation of attn_prefill_kernel
+ * (kernels/attention_prefill.hpp:58-161, launched at src/engine/attention.hip:144) with fp16
+ * queries, fp32 softmax and accumulation, library-chosen geometry. Accuracy: relative L2 ~1e-4
+ * against the fp64 reference on N(0,1) data (fp16 rounding of Q and of the probabilities), where
+ * the fp32-query drop-in kernel reaches 1e-5. Needs n >= 1, pos0 + n <= max_ctx, 16-byte aligned
+ * q / caches / qg rows / core, qg_stride a multiple of 4. */
+typedef struct {
+  const uint16_t* q;       /* fp16 [n][16][256] normalised, rotated queries (unscaled) */
+  const float* qg;         /* gate of (t, h, d) at qg[t * qg_stride + h * 512 + 256 + d] */
+  const uint16_t* k_cache; /* fp16 [2][max_ctx][256], positions [0, pos0 + n) valid */
+  const uint16_t* v_cache;
+  float* core; /* [n][16][256] */
+  unsigned pos0, n, max_ctx, qg_stride;
+} miso_attn_prefill_tc_params;
+
+int miso_attn_prefill_tc(const miso_attn_prefill_tc_params* p, void* stream);
+
+/* attn_prep_batch_kernel (kernels/attention_prefill.hpp:20-40) with the queries written as fp16
+ * to q_f16 [n][16][256] (the input of miso_attn_prefill_tc) instead of fp32 to p->tok0.q, which is
+ * not used. K / V are appended to the fp16 cache exactly as by miso_attn_prep_batch. */
+int miso_attn_prep_batch_f16(const miso_attn_prep_batch_params* p, uint16_t* q_f16, void* stream);
+
 /* ---------------------------------------------------------------------------------------------
  * Library state
  * ------------------------------------------------------------------------------------------- */

@@ -78,6 +78,11 @@ class AttnPrepBatchedParams(C.Structure):
                 ("lens", _P), ("q", _P), ("batch", _U), ("proj_stride", _U), ("eps", _F)]
 
 
+class AttnPrefillTcParams(C.Structure):
+    _fields_ = [("q", _P), ("qg", _P), ("k_cache", _P), ("v_cache", _P), ("core", _P),
+                ("pos0", _U), ("n", _U), ("max_ctx", _U), ("qg_stride", _U)]
+
+
 # name -> (restype, argtypes); every symbol include/miso_cuda.h declares.
 SIGNATURES = {
     "miso_attn_n_splits": (_U, [_U, _U]),
@@ -96,6 +101,8 @@ SIGNATURES = {
     "miso_attn_decode": (C.c_int, [C.POINTER(AttnDecodeParams), _P, C.c_size_t, _P]),
     "miso_attn_decode_noalloc": (C.c_int, [C.POINTER(AttnDecodeParams), _P]),
     "miso_attn_prep_batched": (C.c_int, [C.POINTER(AttnPrepBatchedParams), _P]),
+    "miso_attn_prefill_tc": (C.c_int, [C.POINTER(AttnPrefillTcParams), _P]),
+    "miso_attn_prep_batch_f16": (C.c_int, [C.POINTER(AttnPrepBatchParams), _P, _P]),
     "miso_device_status": (C.c_int, [C.c_int, C.POINTER(C.c_int)]),
     "miso_version": (C.c_char_p, []),
 }

@@ -17,6 +17,7 @@
 
 #include "common/device.cuh"
 #include "fast/attn_decode.cuh"
+#include "fast/attn_prefill_tc.cuh"
 #include "fast/attn_prep.cuh"
 #include "kernels/attention_decode.hpp"
 #include "kernels/attention_prefill.hpp"
@@ -106,9 +107,13 @@ int device_info(DeviceInfo** out) {
       return;
     }
     d.sms = sms;
-    const cudaError_t a = cudaFuncSetAttribute(miso::fast::decode::decode_kernel,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(miso::fast::decode::kSmemBytes));
+    cudaError_t a = cudaFuncSetAttribute(miso::fast::decode::decode_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(miso::fast::decode::kSmemBytes));
+    if (a == cudaSuccess)
+      a = cudaFuncSetAttribute(miso::fast::prefill::prefill_kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(miso::fast::prefill::kSmemBytes));
     d.status = a == cudaSuccess ? MISO_OK : static_cast<int>(a);
   });
   *out = &d;
@@ -134,6 +139,18 @@ int kv_pool_map(CUtensorMap* map, const void* pool, uint64_t rows) {
   const cuuint32_t box[2] = {64, 64};
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(pool),
+                              dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? MISO_OK : MISO_ERR_INVALID;
+}
+
+// fp16 tensor map with a 128-byte swizzle; dims / box innermost first, strides in bytes for
+// dims 1..rank-1.
+int f16_map(CUtensorMap* map, const void* ptr, cuuint32_t rank, const cuuint64_t* dims,
+            const cuuint64_t* strides, const cuuint32_t* box) {
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, rank, const_cast<void*>(ptr),
                               dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -365,6 +382,84 @@ int miso_attn_prep_batched(const miso_attn_prep_batched_params* p, void* stream)
   a.eps = p->eps;
   miso::fast::prep::prep_batched_kernel<<<p->batch, miso::fast::prep::kThreads, 0,
                                            as_stream(stream)>>>(a);
+  return launch_status();
+}
+
+}  // extern "C"
+
+extern "C" {
+
+int miso_attn_prep_batch_f16(const miso_attn_prep_batch_params* p, uint16_t* q_f16,
+                             void* stream) {
+  if (p == nullptr || q_f16 == nullptr || p->tok0.qg == nullptr || p->tok0.k == nullptr ||
+      p->tok0.v == nullptr || p->tok0.q_norm == nullptr || p->tok0.k_norm == nullptr ||
+      p->tok0.inv_freq == nullptr || p->tok0.k_cache == nullptr || p->tok0.v_cache == nullptr ||
+      uint64_t(p->tok0.pos) + p->n > p->tok0.max_ctx || p->proj_stride % 4 != 0 ||
+      !aligned16(p->tok0.qg) || !aligned16(p->tok0.k) || !aligned16(p->tok0.v) ||
+      !aligned16(p->tok0.q_norm) || !aligned16(p->tok0.k_norm) || !aligned16(q_f16) ||
+      !aligned16(p->tok0.k_cache) || !aligned16(p->tok0.v_cache))
+    return MISO_ERR_INVALID;
+  if (p->n == 0)
+    return MISO_OK;
+  miso::fast::prep::PrefillArgs a;
+  a.qg = p->tok0.qg;
+  a.k = p->tok0.k;
+  a.v = p->tok0.v;
+  a.q_norm = p->tok0.q_norm;
+  a.k_norm = p->tok0.k_norm;
+  a.inv_freq = p->tok0.inv_freq;
+  a.k_cache = reinterpret_cast<__half*>(p->tok0.k_cache);
+  a.v_cache = reinterpret_cast<__half*>(p->tok0.v_cache);
+  a.q16 = reinterpret_cast<__half*>(q_f16);
+  a.pos0 = p->tok0.pos;
+  a.max_ctx = p->tok0.max_ctx;
+  a.n = p->n;
+  a.proj_stride = p->proj_stride;
+  a.eps = p->tok0.eps;
+  miso::fast::prep::prefill_prep_kernel<<<p->n, miso::fast::prep::kThreads, 0,
+                                          as_stream(stream)>>>(a);
+  return launch_status();
+}
+
+int miso_attn_prefill_tc(const miso_attn_prefill_tc_params* p, void* stream) {
+  namespace pf = miso::fast::prefill;
+  if (p == nullptr || p->q == nullptr || p->qg == nullptr || p->k_cache == nullptr ||
+      p->v_cache == nullptr || p->core == nullptr || p->n == 0 ||
+      uint64_t(p->pos0) + p->n > p->max_ctx || uint64_t(p->pos0) + p->n >= (uint64_t(1) << 31) ||
+      p->qg_stride % 4 != 0 || !aligned16(p->q) || !aligned16(p->qg) || !aligned16(p->k_cache) ||
+      !aligned16(p->v_cache) || !aligned16(p->core))
+    return MISO_ERR_INVALID;
+  DeviceInfo* d = nullptr;
+  int st = device_info(&d);
+  if (st != MISO_OK)
+    return st;
+  if ((st = tensor_map_encoder()) != MISO_OK)
+    return st;
+  CUtensorMap qmap, kmap, vmap;
+  {
+    const cuuint64_t dims[3] = {256, 16, p->n};
+    const cuuint64_t strides[2] = {256 * 2, 16 * 256 * 2};
+    const cuuint32_t box[3] = {64, 8, 16};
+    if ((st = f16_map(&qmap, p->q, 3, dims, strides, box)) != MISO_OK)
+      return st;
+  }
+  {
+    const cuuint64_t dims[3] = {256, uint64_t(p->pos0) + p->n, 2};
+    const cuuint64_t strides[2] = {256 * 2, uint64_t(p->max_ctx) * 256 * 2};
+    const cuuint32_t box[3] = {64, 64, 1};
+    if ((st = f16_map(&kmap, p->k_cache, 3, dims, strides, box)) != MISO_OK ||
+        (st = f16_map(&vmap, p->v_cache, 3, dims, strides, box)) != MISO_OK)
+      return st;
+  }
+  pf::Args a;
+  a.qg = p->qg;
+  a.core = p->core;
+  a.pos0 = p->pos0;
+  a.n = p->n;
+  a.qg_stride = p->qg_stride;
+  a.n_qtiles = (p->n + pf::kTokens - 1) / pf::kTokens;
+  pf::prefill_kernel<<<2 * a.n_qtiles, pf::kThreads, pf::kSmemBytes, as_stream(stream)>>>(
+      qmap, kmap, vmap, a);
   return launch_status();
 }
 

@@ -1,0 +1,365 @@
+#pragma once
+
+// Causal gated GQA prefill on the 5th-generation tensor cores (tcgen05 + TMEM), the fast path
+// behind miso_attn_prefill_tc().
+//
+// Work item (one CTA): 16 consecutive tokens x the 8 query heads of one KV head = 128 query rows
+// (row r = token (r / 8), head (r % 8)), so every K / V tile is fetched once for all 8 heads that
+// share it. Tiles are launched longest first (the causal triangle makes late tokens the most
+// work), so the block scheduler approximates a longest-processing-time order.
+//
+// Per KV tile j of 64 keys:
+//   S_j = Q K_j^T      tcgen05.mma M=128 N=64 K=256 (16 x K16), fp16 x fp16 -> fp32 in TMEM
+//   softmax            4 warps, one thread per row: TMEM -> registers, causal mask, online max
+//                      (rescaling O only when the max grows by more than 2^8, then exactly),
+//                      P = 2^(s - m) as fp16 into 128B-swizzled shared memory
+//   O += P_j V_j       tcgen05.mma M=128 N=256 K=64 (4 x K16), A = P (K-major), B = V (MN-major)
+// Roles: warp 0 issues TMA (Q once; K, V double-buffered), warp 1 owns TMEM and issues every MMA
+// from one thread, warps 4-7 run softmax, O correction and the epilogue (O / l * sigmoid(gate),
+// each warp staging its 32 rows through shared memory so global stores and gate loads are
+// row-contiguous). Control decisions inside a softmax warp are warp-uniform (__all_sync), as the
+// TMEM accesses are warp-collective.
+//
+// Precision: K / V are the fp16 cache, Q is fp16, P fp16 (bf16 P would cost ~1.6e-3 relative
+// error), all accumulation fp32. Keys past pos0 + n are outside the K / V tensor maps and
+// read as zeros, so garbage beyond the valid cache never reaches the MMAs.
+//
+// Every mbarrier wait is bounded; on a timeout the CTA records MISO_STATUS_TIMEOUT, stops issuing,
+// drains the work it already issued (bounded) and frees its TMEM before exiting.
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "../common/device.cuh"
+#include "../common/tcgen05.cuh"
+
+namespace miso::fast::prefill {
+
+constexpr int kQHeads = 16, kKvHeads = 2, kDim = 256, kGroup = 8;
+constexpr int kTokens = 16;  // tokens per query tile; x 8 heads = 128 rows
+constexpr int kRows = 128;
+constexpr int kBN = 64;  // keys per KV tile
+constexpr int kThreads = 256;
+constexpr uint32_t kQBox = kRows * 64 * 2;      // one 64-dim slab of Q: 16 KB
+constexpr uint32_t kKVBox = kBN * 64 * 2;       // one 64-dim slab of a K / V tile: 8 KB
+constexpr uint32_t kQBytes = 4 * kQBox;         // 64 KB
+constexpr uint32_t kKVBytes = 4 * kKVBox;       // 32 KB
+constexpr uint32_t kPBytes = kRows * kBN * 2;   // 16 KB
+constexpr uint32_t kOffQ = 0;
+constexpr uint32_t kOffK = kOffQ + kQBytes;        // 2 stages
+constexpr uint32_t kOffV = kOffK + 2 * kKVBytes;   // 2 stages
+constexpr uint32_t kOffP = kOffV + 2 * kKVBytes;   // 2 buffers
+constexpr uint32_t kOffBar = kOffP + 2 * kPBytes;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColO = 0;    // O accumulator: 256 columns
+constexpr uint32_t kColS = 256;  // S buffers: 2 x 64 columns
+
+struct Bars {
+  uint64_t q_full;
+  uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
+  uint64_t s_full[2], s_free[2], p_full[2], pv_done[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+constexpr size_t kSmemBytes = 1024 + kOffBar + sizeof(Bars);
+static_assert(kOffK - kOffQ == kQBytes && kOffV - kOffK == 2 * kKVBytes, "layout");
+static_assert(2 * (2 * kKVBytes) == kRows * kDim * 4, "O staging reuses the K and V stages");
+
+struct Args {
+  const float* qg;
+  float* core;
+  unsigned pos0, n, qg_stride, n_qtiles;
+};
+
+__device__ __forceinline__ bool aborted(const Bars& b) {
+  return *reinterpret_cast<const volatile int*>(&b.abort_flag) != 0;
+}
+
+// Bounded wait that also gives up at once if another role has aborted.
+__device__ __forceinline__ bool wait_or_abort(Bars& b, uint64_t& bar, uint32_t parity) {
+  if (aborted(b))
+    return false;
+  if (!dev::mbar_wait(dev::smem_u32(&bar), parity)) {
+    b.abort_flag = 1;
+    return false;
+  }
+  return true;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
+                   const __grid_constant__ CUtensorMap vmap, Args a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  Bars& bar = *reinterpret_cast<Bars*>(base + kOffBar);
+  const unsigned warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const unsigned qt = a.n_qtiles - 1 - blockIdx.x / 2, kvh = blockIdx.x % 2;
+  const unsigned t0 = qt * kTokens;
+  const unsigned nq = min(static_cast<unsigned>(kTokens), a.n - t0);
+  const unsigned key_end = a.pos0 + t0 + nq;  // keys [0, key_end) are seen by some row
+  const unsigned nkv = (key_end + kBN - 1) / kBN;
+  const uint32_t sbase = dev::smem_u32(base);
+
+  if (threadIdx.x == 0) {
+    dev::mbar_init(dev::smem_u32(&bar.q_full), 1);
+    for (int s = 0; s < 2; ++s) {
+      dev::mbar_init(dev::smem_u32(&bar.k_full[s]), 1);
+      dev::mbar_init(dev::smem_u32(&bar.k_empty[s]), 1);
+      dev::mbar_init(dev::smem_u32(&bar.v_full[s]), 1);
+      dev::mbar_init(dev::smem_u32(&bar.v_empty[s]), 1);
+      dev::mbar_init(dev::smem_u32(&bar.s_full[s]), 1);
+      dev::mbar_init(dev::smem_u32(&bar.s_free[s]), 4);
+      dev::mbar_init(dev::smem_u32(&bar.p_full[s]), 4);
+      dev::mbar_init(dev::smem_u32(&bar.pv_done[s]), 1);
+    }
+    dev::mbar_init(dev::smem_u32(&bar.drain), 1);
+    bar.abort_flag = 0;
+    dev::mbar_init_fence();
+  }
+  if (warp == 1) {
+    dev::tmem_alloc(dev::smem_u32(&bar.tmem_base), kTmemCols);
+    dev::tmem_relinquish();
+  }
+  dev::tc_fence_before();
+  __syncthreads();
+  dev::tc_fence_after();
+  const uint32_t tmem = bar.tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------------------ producer
+    if (lane == 0) {
+      dev::tma_prefetch_desc(&qmap);
+      dev::tma_prefetch_desc(&kmap);
+      dev::tma_prefetch_desc(&vmap);
+      dev::mbar_arrive_expect_tx(dev::smem_u32(&bar.q_full), kQBytes);
+      for (int box = 0; box < 4; ++box)
+        dev::tma_load_3d(sbase + kOffQ + box * kQBox, &qmap, box * 64, kvh * kGroup, t0,
+                         dev::smem_u32(&bar.q_full));
+      unsigned issued = 0;
+      for (unsigned j = 0; j < nkv; ++j) {
+        const unsigned s = j & 1, ph = (j >> 1) & 1;
+        if (j >= 2 && !wait_or_abort(bar, bar.k_empty[s], ph ^ 1))
+          break;
+        dev::mbar_arrive_expect_tx(dev::smem_u32(&bar.k_full[s]), kKVBytes);
+        for (int box = 0; box < 4; ++box)
+          dev::tma_load_3d(sbase + kOffK + s * kKVBytes + box * kKVBox, &kmap, box * 64, j * kBN,
+                           kvh, dev::smem_u32(&bar.k_full[s]));
+        if (j >= 2 && !wait_or_abort(bar, bar.v_empty[s], ph ^ 1)) {
+          issued = 2 * j + 1;
+          break;
+        }
+        dev::mbar_arrive_expect_tx(dev::smem_u32(&bar.v_full[s]), kKVBytes);
+        for (int box = 0; box < 4; ++box)
+          dev::tma_load_3d(sbase + kOffV + s * kKVBytes + box * kKVBox, &vmap, box * 64, j * kBN,
+                           kvh, dev::smem_u32(&bar.v_full[s]));
+        issued = 2 * j + 2;
+      }
+      if (aborted(bar)) {
+        // Let the copies already issued land before the CTA exits (bounded waits).
+        dev::mbar_wait(dev::smem_u32(&bar.q_full), 0);
+        for (unsigned c = issued >= 4 ? issued - 4 : 0; c < issued; ++c) {
+          const unsigned j = c / 2, s = j & 1, ph = (j >> 1) & 1;
+          dev::mbar_wait(dev::smem_u32(c % 2 == 0 ? &bar.k_full[s] : &bar.v_full[s]), ph);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------------------ MMA issue
+    if (lane == 0) {
+      const uint32_t idesc_s = dev::idesc_f16_f32(kRows, kBN, 0, 0);
+      const uint32_t idesc_o = dev::idesc_f16_f32(kRows, kDim, 0, 1);
+      bool ok = wait_or_abort(bar, bar.q_full, 0);
+      dev::tc_fence_after();
+      for (unsigned j = 0; ok && j <= nkv; ++j) {
+        if (j < nkv) {
+          const unsigned s = j & 1, ph = (j >> 1) & 1;
+          if (!wait_or_abort(bar, bar.k_full[s], ph) ||
+              (j >= 2 && !wait_or_abort(bar, bar.s_free[s], ph ^ 1))) {
+            ok = false;
+            break;
+          }
+          dev::tc_fence_after();
+          const uint32_t d = tmem + kColS + s * kBN;
+#pragma unroll
+          for (int ks = 0; ks < kDim / 16; ++ks) {
+            const uint64_t ad = dev::sdesc_sw128(sbase + kOffQ + (ks >> 2) * kQBox + (ks & 3) * 32,
+                                                 16, 1024);
+            const uint64_t bd = dev::sdesc_sw128(
+                sbase + kOffK + s * kKVBytes + (ks >> 2) * kKVBox + (ks & 3) * 32, 16, 1024);
+            dev::tc_mma_f16_ss(d, ad, bd, idesc_s, ks > 0);
+          }
+          dev::tc_commit(dev::smem_u32(&bar.s_full[s]));
+          dev::tc_commit(dev::smem_u32(&bar.k_empty[s]));
+        }
+        if (j >= 1) {
+          const unsigned i = j - 1, s = i & 1, ph = (i >> 1) & 1;
+          if (!wait_or_abort(bar, bar.p_full[s], ph) || !wait_or_abort(bar, bar.v_full[s], ph)) {
+            ok = false;
+            break;
+          }
+          dev::tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < kBN / 16; ++kk) {
+            const uint64_t ad = dev::sdesc_sw128(sbase + kOffP + s * kPBytes + kk * 32, 16, 1024);
+            const uint64_t bd =
+                dev::sdesc_sw128(sbase + kOffV + s * kKVBytes + kk * 2048, kKVBox, 1024);
+            dev::tc_mma_f16_ss(tmem + kColO, ad, bd, idesc_o, (i > 0 || kk > 0) ? 1u : 0u);
+          }
+          dev::tc_commit(dev::smem_u32(&bar.pv_done[s]));
+          dev::tc_commit(dev::smem_u32(&bar.v_empty[s]));
+        }
+      }
+      // Every MMA issued above has completed once `drain` flips (bounded).
+      dev::tc_commit(dev::smem_u32(&bar.drain));
+      dev::mbar_wait(dev::smem_u32(&bar.drain), 0);
+    }
+  } else if (warp >= 4) {
+    // --------------------------------------------------------------- softmax and epilogue
+    const unsigned r = (warp - 4) * 32 + lane;
+    const uint32_t trow = tmem + ((32u * (warp & 3)) << 16);
+    const unsigned tok = t0 + r / kGroup;
+    const unsigned pos = a.pos0 + tok;  // this row sees keys [0, pos]
+    const float sl2 = 1.4426950408889634f * 0.0625f;  // log2(e) / sqrt(256)
+    const float kNegInf = -__int_as_float(0x7f800000);
+    float m_ref = kNegInf, l = 0.0f;
+    bool ok = true;
+    for (unsigned j = 0; j < nkv; ++j) {
+      const unsigned s = j & 1, ph = (j >> 1) & 1;
+      if (!__all_sync(0xffffffffu, wait_or_abort(bar, bar.s_full[s], ph))) {
+        ok = false;
+        break;
+      }
+      dev::tc_fence_after();
+      uint32_t x[64];
+      {
+        uint32_t (&x0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&x[0]);
+        uint32_t (&x1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&x[32]);
+        dev::tmem_ld32(trow + kColS + s * kBN, x0);
+        dev::tmem_ld32(trow + kColS + s * kBN + 32, x1);
+        dev::tmem_wait_ld();
+      }
+      dev::tc_fence_before();
+      __syncwarp();
+      if (lane == 0)
+        dev::mbar_arrive(dev::smem_u32(&bar.s_free[s]));
+      const unsigned key0 = j * kBN;
+      float v[64];
+      float mx = kNegInf;
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        v[c] = key0 + c <= pos ? __uint_as_float(x[c]) * sl2 : kNegInf;
+        mx = fmaxf(mx, v[c]);
+      }
+      const float m_new = fmaxf(m_ref, mx);
+      if (j == 0) {
+        m_ref = m_new;  // O is written (not accumulated) by the first P V
+      } else if (__any_sync(0xffffffffu, m_new > m_ref + 8.0f)) {
+        // Rescale O by 2^(m_ref - m_new) once PV_{j-1} has landed; warp-collective TMEM access.
+        const unsigned i = j - 1;
+        if (!__all_sync(0xffffffffu, wait_or_abort(bar, bar.pv_done[i & 1], (i >> 1) & 1))) {
+          ok = false;
+          break;
+        }
+        dev::tc_fence_after();
+        const float corr = exp2f(m_ref - m_new);
+#pragma unroll 1
+        for (int ch = 0; ch < kDim / 32; ++ch) {
+          uint32_t o[32];
+          dev::tmem_ld32(trow + kColO + ch * 32, o);
+          dev::tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            o[e] = __float_as_uint(__uint_as_float(o[e]) * corr);
+          dev::tmem_st32(trow + kColO + ch * 32, o);
+        }
+        dev::tmem_wait_st();
+        l *= corr;
+        m_ref = m_new;
+      }
+      if (j >= 2 &&  // P buffer s is free once PV_{j-2} has completed
+          !__all_sync(0xffffffffu, wait_or_abort(bar, bar.pv_done[s], ph ^ 1))) {
+        ok = false;
+        break;
+      }
+      uint8_t* prow = base + kOffP + s * kPBytes + r * 128;
+      float lsum = 0.0f;
+#pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8) {
+        __align__(16) __half2 h[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          h[e] = __floats2half2_rn(exp2f(v[8 * c8 + 2 * e] - m_ref),
+                                   exp2f(v[8 * c8 + 2 * e + 1] - m_ref));
+          const float2 f = __half22float2(h[e]);
+          lsum += f.x + f.y;
+        }
+        *reinterpret_cast<uint4*>(prow + ((c8 ^ (r & 7)) << 4)) =
+            *reinterpret_cast<const uint4*>(h);
+      }
+      l += lsum;
+      dev::fence_proxy_async_smem();
+      dev::tc_fence_before();
+      __syncwarp();
+      if (lane == 0)
+        dev::mbar_arrive(dev::smem_u32(&bar.p_full[s]));
+    }
+    // ---- epilogue: core = O / l * sigmoid(gate), staged through the (now idle) K/V stages ----
+    const unsigned last = nkv - 1;
+    if (ok && __all_sync(0xffffffffu,
+                         wait_or_abort(bar, bar.pv_done[last & 1], (last >> 1) & 1))) {
+      dev::tc_fence_after();
+      // This warp's 32 rows, [32][256] floats with the float4 index XOR-swizzled by row % 8.
+      float* stage = reinterpret_cast<float*>(base + kOffK) + (warp - 4) * 32 * kDim;
+      const float inv_l = 1.0f / l;
+#pragma unroll 1
+      for (int ch = 0; ch < kDim / 32; ++ch) {
+        uint32_t o[32];
+        dev::tmem_ld32(trow + kColO + ch * 32, o);
+        dev::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const unsigned phys = (ch * 8 + i) ^ (lane & 7);
+          reinterpret_cast<float4*>(stage + lane * kDim)[phys] =
+              make_float4(__uint_as_float(o[4 * i]) * inv_l, __uint_as_float(o[4 * i + 1]) * inv_l,
+                          __uint_as_float(o[4 * i + 2]) * inv_l,
+                          __uint_as_float(o[4 * i + 3]) * inv_l);
+        }
+      }
+      __syncwarp();
+      for (unsigned lr = 0; lr < 32; ++lr) {
+        const unsigned rr = (warp - 4) * 32 + lr;
+        const unsigned tk = t0 + rr / kGroup;
+        if (tk >= a.n)
+          break;
+        const unsigned h = kvh * kGroup + rr % kGroup;
+        const float4* g4 = reinterpret_cast<const float4*>(
+            a.qg + size_t(tk) * a.qg_stride + h * 2 * kDim + kDim);
+        float4* out = reinterpret_cast<float4*>(a.core + (size_t(tk) * kQHeads + h) * kDim);
+        const float4* srow = reinterpret_cast<const float4*>(stage + lr * kDim);
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const unsigned idx = lane + 32 * half;
+          const float4 ov = srow[idx ^ (lr & 7)];
+          const float4 g = g4[idx];
+          out[idx] = make_float4(ov.x / (1.0f + __expf(-g.x)), ov.y / (1.0f + __expf(-g.y)),
+                                 ov.z / (1.0f + __expf(-g.z)), ov.w / (1.0f + __expf(-g.w)));
+        }
+      }
+    }
+  }
+
+  dev::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    dev::tc_fence_after();
+    dev::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+}  // namespace miso::fast::prefill

@@ -57,4 +57,41 @@ __global__ void __launch_bounds__(kThreads) prep_batched_kernel(Args a) {
     a.lens[b] = static_cast<int32_t>(pos + 1);
 }
 
+// Prefill prep for the tensor-core prefill: attn_prep_batch_kernel (kernels/attention_prefill.hpp)
+// with the queries stored as fp16 [n][16][256] (the operand type of the tcgen05 prefill). One block
+// per token, one warp per head; same arithmetic as the drop-in prep up to the final rounding.
+struct PrefillArgs {
+  const float* qg;
+  const float* k;
+  const float* v;
+  const float* q_norm;
+  const float* k_norm;
+  const float* inv_freq;
+  __half* k_cache;
+  __half* v_cache;
+  __half* q16;
+  unsigned pos0, max_ctx, n, proj_stride;
+  float eps;
+};
+
+__global__ void __launch_bounds__(kThreads) prefill_prep_kernel(PrefillArgs a) {
+  using namespace miso::kernels;
+  using namespace miso::kernels::attn;
+  const unsigned t = blockIdx.x, head = threadIdx.x / 32;
+  if (t >= a.n)
+    return;
+  const unsigned pos = a.pos0 + t;
+  const size_t row = size_t(t) * a.proj_stride;
+  if (head < kQHeads) {
+    attn_detail::prep_row_warp(a.qg + row + head * 2 * kDim, a.q_norm, a.inv_freq, pos, a.eps,
+                               nullptr, a.q16 + (size_t(t) * kQHeads + head) * kDim, nullptr,
+                               nullptr);
+  } else {
+    const unsigned kvh = head - kQHeads;
+    const size_t at = (size_t(kvh) * a.max_ctx + pos) * kDim;
+    attn_detail::prep_row_warp(a.k + row + kvh * kDim, a.k_norm, a.inv_freq, pos, a.eps, nullptr,
+                               a.k_cache + at, a.v + row + kvh * kDim, a.v_cache + at);
+  }
+}
+
 }  // namespace miso::fast::prep

@@ -53,9 +53,9 @@ namespace attn_detail {
 
 // One row of 256 (a query head or a key head) on one warp, lane l owning dims [8l, 8l + 8):
 // RMSNorm with `weight`, NEOX rotation of dims [0, 64) at position `pos` (dim d < 32 pairs with
-// d + 32, i.e. lane l < 4 with lane l + 4), then either an fp32 store (out_f32) or an fp16 cache
-// store (out_f16, plus the matching value row v_src -> v_dst). Warp-synchronous, no shared memory,
-// so the drop-in and batched prep kernels produce identical bits.
+// d + 32, i.e. lane l < 4 with lane l + 4), then either an fp32 store (out_f32) or an fp16 store
+// (out_f16, plus the matching value row v_src -> v_dst when v_src is given). Warp-synchronous, no
+// shared memory, so the drop-in and batched prep kernels produce identical bits.
 __device__ __forceinline__ void prep_row_warp(const float* src, const float* weight,
                                               const float* inv_freq, unsigned pos, float eps,
                                               float* out_f32, attn::half_t* out_f16,
@@ -102,6 +102,8 @@ __device__ __forceinline__ void prep_row_warp(const float* src, const float* wei
     for (int i = 0; i < 8; ++i)
       h[i] = __float2half_rn(y[i]);
     reinterpret_cast<uint4*>(out_f16)[lane] = *reinterpret_cast<const uint4*>(h);
+    if (v_src == nullptr)
+      return;
     const float4* v4 = reinterpret_cast<const float4*>(v_src) + 2 * lane;
     const float4 a = v4[0], b = v4[1];
     __align__(16) __half hv[8] = {__float2half_rn(a.x), __float2half_rn(a.y),

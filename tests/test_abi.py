@@ -46,6 +46,7 @@ def test_ctypes_structs_match_the_c_header():
         "miso_deltanet_chunk_params": capi.DeltaNetChunkParams,
         "miso_attn_decode_params": capi.AttnDecodeParams,
         "miso_attn_prep_batched_params": capi.AttnPrepBatchedParams,
+        "miso_attn_prefill_tc_params": capi.AttnPrefillTcParams,
     }
     lines = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{HEADER}"', "int main(){"]
     for cname, py in structs.items():

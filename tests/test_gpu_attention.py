@@ -348,3 +348,69 @@ def test_engine_decode_sequence_matches_oracle():
         assert rel_per_head(core.cpu().numpy(), ref) <= 1e-5
         assert rel_per_head(sc.q.cpu().numpy(), rq) <= 2e-6
     assert cache.len == 40
+
+
+# ---- causal prefill on tcgen05 (fp16 queries; BASELINE bar: rel-L2 <= 1e-3, max-abs <= 1e-2) ---
+
+
+def run_prefill_tc(q16, qg, k, v, pos0, n, max_ctx):
+    core = torch.full((n, 16, 256), -3.0, device=DEV)
+    dq, dqg, dk, dv = T(q16), T(qg), T(k), T(v)
+    p = capi.AttnPrefillTcParams(ptr(dq), ptr(dqg), ptr(dk), ptr(dv), ptr(core), pos0, n, max_ctx,
+                                 16 * 512)
+    capi.check("miso_attn_prefill_tc", capi.load().miso_attn_prefill_tc(C.byref(p), None))
+    torch.cuda.synchronize()
+    return core.cpu().numpy()
+
+
+@pytest.mark.parametrize("pos0,n", [(0, 1), (0, 15), (0, 16), (0, 17), (0, 100), (40, 17),
+                                    (300, 77), (0, 512), (1000, 333), (0, 2048)])
+def test_prefill_tc_matches_fp64(pos0, n):
+    length = pos0 + n
+    max_ctx = length + 5
+    rng = np.random.RandomState(7000 + 13 * pos0 + n)
+    q16 = rng.standard_normal((n, 16, 256)).astype(np.float16)
+    qg = rng.standard_normal((n, 16, 512)).astype(np.float32)
+    k = rng.standard_normal((2, max_ctx, 256)).astype(np.float16)
+    v = rng.standard_normal((2, max_ctx, 256)).astype(np.float16)
+    k[:, length:] = np.float16(np.nan)  # never read: outside the tensor maps
+    v[:, length:] = np.float16(np.nan)
+    got = run_prefill_tc(q16, qg, k, v, pos0, n, max_ctx)
+    ref = oracle.attn_prefill(n, pos0, q16.astype(np.float32), qg, 8192, k.view(np.uint16),
+                              v.view(np.uint16), max_ctx)
+    assert rel_per_head(got, ref) <= 1e-3
+    assert np.abs(got - ref).max() <= 1e-2
+    # logits-proxy argmax over each output row is exact wherever the oracle's top-2 gap clears the
+    # error bound
+    srt = np.sort(ref.reshape(-1, 256), axis=1)
+    clear = (srt[:, -1] - srt[:, -2]) > 2e-3
+    assert clear.mean() > 0.5
+    assert np.array_equal(got.reshape(-1, 256)[clear].argmax(1), ref.reshape(-1, 256)[clear].argmax(1))
+
+
+def test_prep_batch_f16_matches_drop_in_prep():
+    n, pos0, max_ctx = 37, 11, 64
+    rng = np.random.RandomState(77)
+    proj = (rng.standard_normal((n, 9216))).astype(np.float32)
+    qn = (1 + 0.1 * rng.standard_normal(256)).astype(np.float32)
+    kn = (1 + 0.1 * rng.standard_normal(256)).astype(np.float32)
+    dproj, dqn, dkn, dinv = T(proj), T(qn), T(kn), T(A.rope_inv_freq())
+    caches = []
+    for f16 in (False, True):
+        kc = torch.zeros((2, max_ctx, 256), dtype=torch.float16, device=DEV)
+        vc = torch.zeros_like(kc)
+        q32 = torch.zeros((n, 16, 256), device=DEV)
+        q16 = torch.zeros((n, 16, 256), dtype=torch.float16, device=DEV)
+        base = ptr(dproj)
+        tok0 = capi.AttnPrepParams(base, base + 8192 * 4, base + 8704 * 4, ptr(dqn), ptr(dkn),
+                                   ptr(dinv), ptr(kc), ptr(vc), ptr(q32), pos0, max_ctx, 1e-6)
+        bp = capi.AttnPrepBatchParams(tok0, n, 9216)
+        if f16:
+            capi.check("f16", capi.load().miso_attn_prep_batch_f16(C.byref(bp), ptr(q16), None))
+        else:
+            A.attn_prep_batch(bp)
+        torch.cuda.synchronize()
+        caches.append((kc.clone(), vc.clone(), q32.clone(), q16.clone()))
+    (k0, v0, q32, _), (k1, v1, _, q16) = caches
+    assert torch.equal(k0, k1) and torch.equal(v0, v1)
+    assert torch.equal(q32.half(), q16)
