@@ -368,7 +368,7 @@ def bench_prefill(args, dev, stream, max_over_ranks, barrier, world) -> dict:
     from miso_b200 import attention as A
     from miso_b200 import capi
 
-    n = PREFILL_N
+    n = args.prefill_n
     g = torch.Generator(device=dev)
     g.manual_seed(99)
     proj = torch.randn((n, PROJ), generator=g, device=dev).bfloat16().float()  # bf16 values
@@ -415,7 +415,7 @@ def bench_prefill(args, dev, stream, max_over_ranks, barrier, world) -> dict:
     flops = prefill_flops(n)
     pk = peaks()
     achieved = flops / (kern_ms * 1e-3) / 1e12
-    return {"metric": "prefill TFLOP/s @8k", "value": world * flops / (step_ms * 1e-3) / 1e12,
+    return {"metric": f"prefill TFLOP/s @{n}", "value": world * flops / (step_ms * 1e-3) / 1e12,
             "unit": "TFLOP/s", "ms_per_step": step_ms, "n_tokens": n,
             "config": "BASELINE config 3: 1 x 8192 tokens per GPU, causal, 16 Q / 2 KV heads, "
                       "d 256, RoPE 64 dims theta 1e7, sigmoid gate, bf16 inputs, fp16 tensor "
@@ -438,6 +438,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true",
                     help="skip the prefill leg (BASELINE config 3) of the JSON line")
+    ap.add_argument("--prefill-n", type=int, default=PREFILL_N,
+                    help="prefill tokens (default 8192, the BASELINE config; smaller only for "
+                         "profiling captures)")
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="sequences per GPU (default 32, the BASELINE config; smaller only for "
                          "profiling captures)")

@@ -119,6 +119,13 @@ __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// 2^x on the special-function unit (approximate, flushes subnormals; 2^-inf = +0).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // ---- 3-D TMA tile load --------------------------------------------------------------------------
 
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* map, int x, int y, int z,

@@ -10,12 +10,14 @@
 //
 // Per KV tile j of 64 keys:
 //   S_j = Q K_j^T      tcgen05.mma M=128 N=64 K=256 (16 x K16), fp16 x fp16 -> fp32 in TMEM
-//   softmax            4 warps, one thread per row: TMEM -> registers, causal mask, online max
-//                      (rescaling O only when the max grows by more than 2^8, then exactly),
-//                      P = 2^(s - m) as fp16 into 128B-swizzled shared memory
+//   softmax            8 warps, two per TMEM lane quadrant (one thread per row and half of the
+//                      tile's columns; the pair exchanges row maxima through shared memory):
+//                      causal mask on diagonal tiles only, online max (rescaling O only when
+//                      the max grows by more than 2^8, then exactly), P = 2^(s - m) as fp16
+//                      into 128B-swizzled shared memory
 //   O += P_j V_j       tcgen05.mma M=128 N=256 K=64 (4 x K16), A = P (K-major), B = V (MN-major)
 // Roles: warp 0 issues TMA (Q once; K, V double-buffered), warp 1 owns TMEM and issues every MMA
-// from one thread, warps 4-7 run softmax, O correction and the epilogue (O / l * sigmoid(gate),
+// from one thread, warps 4-11 run softmax, O correction and the epilogue (O / l * sigmoid(gate),
 // each warp staging its 32 rows through shared memory so global stores and gate loads are
 // row-contiguous). Control decisions inside a softmax warp are warp-uniform (__all_sync), as the
 // TMEM accesses are warp-collective.
@@ -42,7 +44,7 @@ constexpr int kQHeads = 16, kKvHeads = 2, kDim = 256, kGroup = 8;
 constexpr int kTokens = 16;  // tokens per query tile; x 8 heads = 128 rows
 constexpr int kRows = 128;
 constexpr int kBN = 64;  // keys per KV tile
-constexpr int kThreads = 256;
+constexpr int kThreads = 384;  // warp 0 TMA, warp 1 MMA + TMEM, warps 4-11 softmax
 constexpr uint32_t kQBox = kRows * 64 * 2;      // one 64-dim slab of Q: 16 KB
 constexpr uint32_t kKVBox = kBN * 64 * 2;       // one 64-dim slab of a K / V tile: 8 KB
 constexpr uint32_t kQBytes = 4 * kQBox;         // 64 KB
@@ -52,7 +54,8 @@ constexpr uint32_t kOffQ = 0;
 constexpr uint32_t kOffK = kOffQ + kQBytes;        // 2 stages
 constexpr uint32_t kOffV = kOffK + 2 * kKVBytes;   // 2 stages
 constexpr uint32_t kOffP = kOffV + 2 * kKVBytes;   // 2 buffers
-constexpr uint32_t kOffBar = kOffP + 2 * kPBytes;
+constexpr uint32_t kOffRed = kOffP + 2 * kPBytes;  // [2 parity][2 column half][128 rows] f32
+constexpr uint32_t kOffBar = kOffRed + 2 * 2 * kRows * 4;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 0;    // O accumulator: 256 columns
 constexpr uint32_t kColS = 256;  // S buffers: 2 x 64 columns
@@ -61,12 +64,13 @@ struct Bars {
   uint64_t q_full;
   uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
   uint64_t s_full[2], s_free[2], p_full[2], pv_done[2];
+  uint64_t xchg[4][2];  // per TMEM lane quadrant and tile parity: the two softmax warps' partials
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
 };
 
-constexpr size_t kSmemBytes = 1024 + kOffBar + sizeof(Bars);
+constexpr size_t kSmemBytes = kOffBar + sizeof(Bars);  // base must be 1024-byte aligned
 static_assert(kOffK - kOffQ == kQBytes && kOffV - kOffK == 2 * kKVBytes, "layout");
 static_assert(2 * (2 * kKVBytes) == kRows * kDim * 4, "O staging reuses the K and V stages");
 
@@ -94,9 +98,13 @@ __device__ __forceinline__ bool wait_or_abort(Bars& b, uint64_t& bar, uint32_t p
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                    const __grid_constant__ CUtensorMap vmap, Args a) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* base = smem_raw;
+  if ((dev::smem_u32(base) & 1023u) != 0) {  // the 128-byte swizzle needs 1024-byte alignment
+    if (threadIdx.x == 0)
+      dev::set_status(dev::kStatusTimeout);
+    return;
+  }
   Bars& bar = *reinterpret_cast<Bars*>(base + kOffBar);
   const unsigned warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const unsigned qt = a.n_qtiles - 1 - blockIdx.x / 2, kvh = blockIdx.x % 2;
@@ -114,9 +122,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       dev::mbar_init(dev::smem_u32(&bar.v_full[s]), 1);
       dev::mbar_init(dev::smem_u32(&bar.v_empty[s]), 1);
       dev::mbar_init(dev::smem_u32(&bar.s_full[s]), 1);
-      dev::mbar_init(dev::smem_u32(&bar.s_free[s]), 4);
-      dev::mbar_init(dev::smem_u32(&bar.p_full[s]), 4);
+      dev::mbar_init(dev::smem_u32(&bar.s_free[s]), 8);
+      dev::mbar_init(dev::smem_u32(&bar.p_full[s]), 8);
       dev::mbar_init(dev::smem_u32(&bar.pv_done[s]), 1);
+      for (int qd = 0; qd < 4; ++qd)
+        dev::mbar_init(dev::smem_u32(&bar.xchg[qd][s]), 64);
     }
     dev::mbar_init(dev::smem_u32(&bar.drain), 1);
     bar.abort_flag = 0;
@@ -174,6 +184,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       const uint32_t idesc_s = dev::idesc_f16_f32(kRows, kBN, 0, 0);
       const uint32_t idesc_o = dev::idesc_f16_f32(kRows, kDim, 0, 1);
+      // Descriptors of buffer 0 at k-offset 0; offsets are added to the start-address field.
+      const uint64_t qdesc0 = dev::sdesc_sw128(sbase + kOffQ, 16, 1024);
+      const uint64_t kdesc0 = dev::sdesc_sw128(sbase + kOffK, 16, 1024);
+      const uint64_t pdesc0 = dev::sdesc_sw128(sbase + kOffP, 16, 1024);
+      const uint64_t vdesc0 = dev::sdesc_sw128(sbase + kOffV, kKVBox, 1024);
       bool ok = wait_or_abort(bar, bar.q_full, 0);
       dev::tc_fence_after();
       for (unsigned j = 0; ok && j <= nkv; ++j) {
@@ -186,14 +201,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           dev::tc_fence_after();
           const uint32_t d = tmem + kColS + s * kBN;
+          const uint64_t kd = kdesc0 + ((s * kKVBytes) >> 4);
 #pragma unroll
-          for (int ks = 0; ks < kDim / 16; ++ks) {
-            const uint64_t ad = dev::sdesc_sw128(sbase + kOffQ + (ks >> 2) * kQBox + (ks & 3) * 32,
-                                                 16, 1024);
-            const uint64_t bd = dev::sdesc_sw128(
-                sbase + kOffK + s * kKVBytes + (ks >> 2) * kKVBox + (ks & 3) * 32, 16, 1024);
-            dev::tc_mma_f16_ss(d, ad, bd, idesc_s, ks > 0);
-          }
+          for (int ks = 0; ks < kDim / 16; ++ks)
+            dev::tc_mma_f16_ss(d, qdesc0 + (((ks >> 2) * kQBox + (ks & 3) * 32) >> 4),
+                               kd + (((ks >> 2) * kKVBox + (ks & 3) * 32) >> 4), idesc_s, ks > 0);
           dev::tc_commit(dev::smem_u32(&bar.s_full[s]));
           dev::tc_commit(dev::smem_u32(&bar.k_empty[s]));
         }
@@ -204,13 +216,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           dev::tc_fence_after();
+          const uint64_t pd = pdesc0 + ((s * kPBytes) >> 4), vd = vdesc0 + ((s * kKVBytes) >> 4);
 #pragma unroll
-          for (int kk = 0; kk < kBN / 16; ++kk) {
-            const uint64_t ad = dev::sdesc_sw128(sbase + kOffP + s * kPBytes + kk * 32, 16, 1024);
-            const uint64_t bd =
-                dev::sdesc_sw128(sbase + kOffV + s * kKVBytes + kk * 2048, kKVBox, 1024);
-            dev::tc_mma_f16_ss(tmem + kColO, ad, bd, idesc_o, (i > 0 || kk > 0) ? 1u : 0u);
-          }
+          for (int kk = 0; kk < kBN / 16; ++kk)
+            dev::tc_mma_f16_ss(tmem + kColO, pd + ((kk * 32) >> 4), vd + ((kk * 2048) >> 4),
+                               idesc_o, (i > 0 || kk > 0) ? 1u : 0u);
           dev::tc_commit(dev::smem_u32(&bar.pv_done[s]));
           dev::tc_commit(dev::smem_u32(&bar.v_empty[s]));
         }
@@ -221,14 +231,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= 4) {
     // --------------------------------------------------------------- softmax and epilogue
-    const unsigned r = (warp - 4) * 32 + lane;
-    const uint32_t trow = tmem + ((32u * (warp & 3)) << 16);
+    // Two warps per TMEM lane quadrant: warp (4 + q + 4 hc) holds rows [32 q, 32 q + 32) and
+    // S columns [32 hc, 32 hc + 32) of each tile, O columns [128 hc, 128 hc + 128).
+    const unsigned q = warp & 3, hc = (warp - 4) >> 2;
+    const unsigned r = 32 * q + lane;
+    const uint32_t trow = tmem + ((32u * q) << 16);
     const unsigned tok = t0 + r / kGroup;
-    const unsigned pos = a.pos0 + tok;  // this row sees keys [0, pos]
+    const unsigned pos = a.pos0 + tok;        // this row sees keys [0, pos]
+    const unsigned pos_min = a.pos0 + t0;     // no row of the tile sees fewer keys
+    float* red = reinterpret_cast<float*>(base + kOffRed);
     const float sl2 = 1.4426950408889634f * 0.0625f;  // log2(e) / sqrt(256)
     const float kNegInf = -__int_as_float(0x7f800000);
     float m_ref = kNegInf, l = 0.0f;
     bool ok = true;
+    // Exchange of one float per row with the partner warp through red[] and an mbarrier of
+    // 64 arrivals (bounded wait); returns the partner's value.
+    auto exchange = [&](unsigned j, float mine, float& theirs) -> bool {
+      red[((j & 1) * 2 + hc) * kRows + r] = mine;
+      dev::mbar_arrive(dev::smem_u32(&bar.xchg[q][j & 1]));
+      if (!__all_sync(0xffffffffu, wait_or_abort(bar, bar.xchg[q][j & 1], (j >> 1) & 1)))
+        return false;
+      theirs = red[((j & 1) * 2 + (1 - hc)) * kRows + r];
+      return true;
+    };
     for (unsigned j = 0; j < nkv; ++j) {
       const unsigned s = j & 1, ph = (j >> 1) & 1;
       if (!__all_sync(0xffffffffu, wait_or_abort(bar, bar.s_full[s], ph))) {
@@ -236,47 +261,56 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       dev::tc_fence_after();
-      uint32_t x[64];
-      {
-        uint32_t (&x0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&x[0]);
-        uint32_t (&x1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&x[32]);
-        dev::tmem_ld32(trow + kColS + s * kBN, x0);
-        dev::tmem_ld32(trow + kColS + s * kBN + 32, x1);
-        dev::tmem_wait_ld();
-      }
+      uint32_t x[32];
+      dev::tmem_ld32(trow + kColS + s * kBN + 32 * hc, x);
+      dev::tmem_wait_ld();
       dev::tc_fence_before();
       __syncwarp();
       if (lane == 0)
         dev::mbar_arrive(dev::smem_u32(&bar.s_free[s]));
-      const unsigned key0 = j * kBN;
-      float v[64];
+      const unsigned key0 = j * kBN + 32 * hc;
+      float v[32];
       float mx = kNegInf;
+      if (key0 + 31 <= pos_min) {  // interior tile half: no masking
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        v[c] = key0 + c <= pos ? __uint_as_float(x[c]) * sl2 : kNegInf;
-        mx = fmaxf(mx, v[c]);
+        for (int c = 0; c < 32; ++c) {
+          v[c] = __uint_as_float(x[c]) * sl2;
+          mx = fmaxf(mx, v[c]);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          v[c] = key0 + c <= pos ? __uint_as_float(x[c]) * sl2 : kNegInf;
+          mx = fmaxf(mx, v[c]);
+        }
       }
-      const float m_new = fmaxf(m_ref, mx);
+      float mx_other;
+      if (!exchange(j, mx, mx_other)) {
+        ok = false;
+        break;
+      }
+      const float m_new = fmaxf(m_ref, fmaxf(mx, mx_other));
       if (j == 0) {
         m_ref = m_new;  // O is written (not accumulated) by the first P V
       } else if (__any_sync(0xffffffffu, m_new > m_ref + 8.0f)) {
-        // Rescale O by 2^(m_ref - m_new) once PV_{j-1} has landed; warp-collective TMEM access.
+        // Both warps of the pair see the same rows and maxima, so they take this branch
+        // together; each rescales its 128 O columns once PV_{j-1} has landed.
         const unsigned i = j - 1;
         if (!__all_sync(0xffffffffu, wait_or_abort(bar, bar.pv_done[i & 1], (i >> 1) & 1))) {
           ok = false;
           break;
         }
         dev::tc_fence_after();
-        const float corr = exp2f(m_ref - m_new);
+        const float corr = dev::ex2_approx(m_ref - m_new);
 #pragma unroll 1
-        for (int ch = 0; ch < kDim / 32; ++ch) {
+        for (int ch = 0; ch < 4; ++ch) {
           uint32_t o[32];
-          dev::tmem_ld32(trow + kColO + ch * 32, o);
+          dev::tmem_ld32(trow + kColO + 128 * hc + ch * 32, o);
           dev::tmem_wait_ld();
 #pragma unroll
           for (int e = 0; e < 32; ++e)
             o[e] = __float_as_uint(__uint_as_float(o[e]) * corr);
-          dev::tmem_st32(trow + kColO + ch * 32, o);
+          dev::tmem_st32(trow + kColO + 128 * hc + ch * 32, o);
         }
         dev::tmem_wait_st();
         l *= corr;
@@ -290,16 +324,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint8_t* prow = base + kOffP + s * kPBytes + r * 128;
       float lsum = 0.0f;
 #pragma unroll
-      for (int c8 = 0; c8 < 8; ++c8) {
+      for (int c4 = 0; c4 < 4; ++c4) {
         __align__(16) __half2 h[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          h[e] = __floats2half2_rn(exp2f(v[8 * c8 + 2 * e] - m_ref),
-                                   exp2f(v[8 * c8 + 2 * e + 1] - m_ref));
-          const float2 f = __half22float2(h[e]);
-          lsum += f.x + f.y;
+          const float p0 = dev::ex2_approx(v[8 * c4 + 2 * e] - m_ref);
+          const float p1 = dev::ex2_approx(v[8 * c4 + 2 * e + 1] - m_ref);
+          h[e] = __floats2half2_rn(p0, p1);
+          lsum += p0 + p1;
         }
-        *reinterpret_cast<uint4*>(prow + ((c8 ^ (r & 7)) << 4)) =
+        *reinterpret_cast<uint4*>(prow + (((4 * hc + c4) ^ (r & 7)) << 4)) =
             *reinterpret_cast<const uint4*>(h);
       }
       l += lsum;
@@ -311,21 +345,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     // ---- epilogue: core = O / l * sigmoid(gate), staged through the (now idle) K/V stages ----
     const unsigned last = nkv - 1;
-    if (ok && __all_sync(0xffffffffu,
-                         wait_or_abort(bar, bar.pv_done[last & 1], (last >> 1) & 1))) {
+    float l_other = 0.0f;
+    if (ok && exchange(nkv, l, l_other) &&
+        __all_sync(0xffffffffu, wait_or_abort(bar, bar.pv_done[last & 1], (last >> 1) & 1))) {
       dev::tc_fence_after();
-      // This warp's 32 rows, [32][256] floats with the float4 index XOR-swizzled by row % 8.
-      float* stage = reinterpret_cast<float*>(base + kOffK) + (warp - 4) * 32 * kDim;
-      const float inv_l = 1.0f / l;
+      // This warp's 32 rows x 128 columns, float4 index XOR-swizzled by row % 8.
+      float* stage = reinterpret_cast<float*>(base + kOffK) + (warp - 4) * 32 * 128;
+      const float inv_l = 1.0f / (l + l_other);
 #pragma unroll 1
-      for (int ch = 0; ch < kDim / 32; ++ch) {
+      for (int ch = 0; ch < 4; ++ch) {
         uint32_t o[32];
-        dev::tmem_ld32(trow + kColO + ch * 32, o);
+        dev::tmem_ld32(trow + kColO + 128 * hc + ch * 32, o);
         dev::tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const unsigned phys = (ch * 8 + i) ^ (lane & 7);
-          reinterpret_cast<float4*>(stage + lane * kDim)[phys] =
+          reinterpret_cast<float4*>(stage + lane * 128)[phys] =
               make_float4(__uint_as_float(o[4 * i]) * inv_l, __uint_as_float(o[4 * i + 1]) * inv_l,
                           __uint_as_float(o[4 * i + 2]) * inv_l,
                           __uint_as_float(o[4 * i + 3]) * inv_l);
@@ -333,23 +368,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncwarp();
       for (unsigned lr = 0; lr < 32; ++lr) {
-        const unsigned rr = (warp - 4) * 32 + lr;
+        const unsigned rr = 32 * q + lr;
         const unsigned tk = t0 + rr / kGroup;
         if (tk >= a.n)
           break;
         const unsigned h = kvh * kGroup + rr % kGroup;
-        const float4* g4 = reinterpret_cast<const float4*>(
-            a.qg + size_t(tk) * a.qg_stride + h * 2 * kDim + kDim);
-        float4* out = reinterpret_cast<float4*>(a.core + (size_t(tk) * kQHeads + h) * kDim);
-        const float4* srow = reinterpret_cast<const float4*>(stage + lr * kDim);
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          const unsigned idx = lane + 32 * half;
-          const float4 ov = srow[idx ^ (lr & 7)];
-          const float4 g = g4[idx];
-          out[idx] = make_float4(ov.x / (1.0f + __expf(-g.x)), ov.y / (1.0f + __expf(-g.y)),
-                                 ov.z / (1.0f + __expf(-g.z)), ov.w / (1.0f + __expf(-g.w)));
-        }
+        const float4 ov = reinterpret_cast<const float4*>(stage + lr * 128)[lane ^ (lr & 7)];
+        const float4 g = reinterpret_cast<const float4*>(
+            a.qg + size_t(tk) * a.qg_stride + h * 2 * kDim + kDim + 128 * hc)[lane];
+        reinterpret_cast<float4*>(a.core + (size_t(tk) * kQHeads + h) * kDim + 128 * hc)[lane] =
+            make_float4(ov.x / (1.0f + __expf(-g.x)), ov.y / (1.0f + __expf(-g.y)),
+                        ov.z / (1.0f + __expf(-g.z)), ov.w / (1.0f + __expf(-g.w)));
       }
     }
   }
