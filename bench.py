@@ -299,6 +299,8 @@ def run_miso(args) -> None:
 
     prefill = None if args.no_prefill else bench_prefill(args, dev, stream, max_over_ranks,
                                                          barrier, world)
+    dn_step = None if args.no_deltanet else bench_deltanet_step(args, dev, stream,
+                                                                max_over_ranks, barrier, world)
 
     st = ctypes.c_int(-1)
     capi.check("miso_device_status", capi.load().miso_device_status(1, st))
@@ -348,6 +350,7 @@ def run_miso(args) -> None:
         "clocks": clk.summary(),
         "cpu_baseline": cpu,
         "prefill": prefill,
+        "deltanet_step": dn_step,
     }
     print(json.dumps(line), flush=True)
 
@@ -428,6 +431,72 @@ def bench_prefill(args, dev, stream, max_over_ranks, barrier, world) -> dict:
             "gpu_launches": 2 * args.steps}
 
 
+DN_BATCH = 64
+DN_STATE_BYTES = 32 * 128 * 128 * 4
+DN_PROJ = 12352  # [qkv 8192 | z 4096 | a 32 | b 32]
+
+
+def bench_deltanet_step(args, dev, stream, max_over_ranks, barrier, world) -> dict:
+    """BASELINE config 4b: one Gated DeltaNet decode step for 64 sequences per GPU on fp32
+    [32][128][128] states (zero-initialised), qkv / z / a / b N(0,1) bf16 values, conv_w
+    N(0, 0.5), ssm_a = -1, dt_bias = 0. HBM-bound: algorithmic bytes per step = state read +
+    write (268 MB) + conv history read + write + inputs + outputs."""
+    import torch
+    from miso_b200 import capi
+
+    B = DN_BATCH
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    proj = torch.randn((B, DN_PROJ), generator=g, device=dev).bfloat16().float()
+    conv_w = 0.5 * torch.randn((8192, 4), generator=g, device=dev)
+    ssm_a = -torch.ones(32, device=dev)
+    dt = torch.zeros(32, device=dev)
+    norm_w = torch.ones(128, device=dev)
+    conv = [torch.zeros((B, 8192, 3), device=dev) for _ in range(2)]
+    state = torch.zeros((B, 32, 128, 128), device=dev)
+    out = torch.empty((B, 4096), device=dev)
+    lib = capi.load()
+    base = proj.data_ptr()
+    params = [capi.DeltaNetStepBatchedParams(base, base + 8192 * 4, base + 12288 * 4,
+                                             base + 12320 * 4, conv_w.data_ptr(),
+                                             ssm_a.data_ptr(), dt.data_ptr(), norm_w.data_ptr(),
+                                             conv[i].data_ptr(), conv[1 - i].data_ptr(),
+                                             state.data_ptr(), out.data_ptr(), B, DN_PROJ, EPS)
+              for i in range(2)]
+
+    def step(i):
+        capi.check("dn_step", lib.miso_deltanet_step_batched(ctypes.byref(params[i % 2]),
+                                                             stream.cuda_stream))
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    nbytes = (2 * B * DN_STATE_BYTES + 2 * B * 8192 * 3 * 4 + B * DN_PROJ * 4 + B * 4096 * 4 +
+              8192 * 4 * 4)
+    achieved = nbytes / (ms * 1e-3) / 1e9
+    pk = peaks()
+    return {"metric": "DeltaNet decode tok/s (batch 64)", "value": world * B / (ms * 1e-3),
+            "unit": "tokens/s", "ms_per_step": ms,
+            "config": "BASELINE config 4b: 64 sequences per GPU, 16 K / 32 V heads, d 128, fp32 "
+                      "states (zero-init), bf16-valued inputs; one launch per step",
+            "bytes_per_step": nbytes,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"],
+                         "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "traffic": None,
+                         "kernel": "step_batched_kernel", "kernel_ms": ms,
+                         "peak_source": pk["source"]},
+            "gpu_launches": args.steps}
+
+
 def main():
     global BATCH
     ap = argparse.ArgumentParser()
@@ -438,6 +507,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true",
                     help="skip the prefill leg (BASELINE config 3) of the JSON line")
+    ap.add_argument("--no-deltanet", action="store_true",
+                    help="skip the DeltaNet legs (BASELINE config 4) of the JSON line")
     ap.add_argument("--prefill-n", type=int, default=PREFILL_N,
                     help="prefill tokens (default 8192, the BASELINE config; smaller only for "
                          "profiling captures)")

@@ -47,7 +47,9 @@ enum {
   MISO_ERR_LIMIT = -5      /* request exceeds a fixed capacity (miso_attn_decode_noalloc) */
 };
 
-/* Device status word (miso_device_status). */
+/* Device status word (miso_device_status): the first failure recorded on the device. Low byte:
+ * MISO_STATUS_*; bits 8 and up: the kernel wait site that recorded it (0x11-0x13 batched decode,
+ * 0x20 tensor-core prefill). */
 enum { MISO_STATUS_OK = 0, MISO_STATUS_TIMEOUT = 1 };
 
 /* ---------------------------------------------------------------------------------------------
@@ -293,6 +295,32 @@ int miso_attn_prefill_tc(const miso_attn_prefill_tc_params* p, void* stream);
  * to q_f16 [n][16][256] (the input of miso_attn_prefill_tc) instead of fp32 to p->tok0.q, which is
  * not used. K / V are appended to the fp16 cache exactly as by miso_attn_prep_batch. */
 int miso_attn_prep_batch_f16(const miso_attn_prep_batch_params* p, uint16_t* q_f16, void* stream);
+
+/* Batched Gated DeltaNet decode step: deltanet_step_kernel (kernels/deltanet_step.hpp:65-140,
+ * launched at src/engine/deltanet.hip:79) for `batch` independent sequences in one launch.
+ * Sequence b's inputs are the rows qkv / z / a / b + b * in_stride (8192 / 4096 / 32 / 32 values;
+ * in_stride = 12352 for the engine's [qkv | z | a | b] projection rows); its conv history
+ * [8192][3] at conv_in / conv_out + b * 24576 (double-buffered: conv_in != conv_out), its state
+ * [32][128][128] at state + b * 524288 (updated in place), its output at out + b * 4096.
+ * Weights (conv_w [8192][4], ssm_a, dt_bias [32], norm_w [128]) are shared. */
+typedef struct {
+  const float* qkv;
+  const float* z;
+  const float* a;
+  const float* b;
+  const float* conv_w;
+  const float* ssm_a;
+  const float* dt_bias;
+  const float* norm_w;
+  const float* conv_in;
+  float* conv_out;
+  float* state;
+  float* out;
+  unsigned batch, in_stride;
+  float eps;
+} miso_deltanet_step_batched_params;
+
+int miso_deltanet_step_batched(const miso_deltanet_step_batched_params* p, void* stream);
 
 /* ---------------------------------------------------------------------------------------------
  * Library state

@@ -83,6 +83,12 @@ class AttnPrefillTcParams(C.Structure):
                 ("pos0", _U), ("n", _U), ("max_ctx", _U), ("qg_stride", _U)]
 
 
+class DeltaNetStepBatchedParams(C.Structure):
+    _fields_ = [("qkv", _P), ("z", _P), ("a", _P), ("b", _P), ("conv_w", _P), ("ssm_a", _P),
+                ("dt_bias", _P), ("norm_w", _P), ("conv_in", _P), ("conv_out", _P),
+                ("state", _P), ("out", _P), ("batch", _U), ("in_stride", _U), ("eps", _F)]
+
+
 # name -> (restype, argtypes); every symbol include/miso_cuda.h declares.
 SIGNATURES = {
     "miso_attn_n_splits": (_U, [_U, _U]),
@@ -102,6 +108,7 @@ SIGNATURES = {
     "miso_attn_decode_noalloc": (C.c_int, [C.POINTER(AttnDecodeParams), _P]),
     "miso_attn_prep_batched": (C.c_int, [C.POINTER(AttnPrepBatchedParams), _P]),
     "miso_attn_prefill_tc": (C.c_int, [C.POINTER(AttnPrefillTcParams), _P]),
+    "miso_deltanet_step_batched": (C.c_int, [C.POINTER(DeltaNetStepBatchedParams), _P]),
     "miso_attn_prep_batch_f16": (C.c_int, [C.POINTER(AttnPrepBatchParams), _P, _P]),
     "miso_device_status": (C.c_int, [C.c_int, C.POINTER(C.c_int)]),
     "miso_version": (C.c_char_p, []),

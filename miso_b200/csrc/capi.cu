@@ -19,6 +19,7 @@
 #include "fast/attn_decode.cuh"
 #include "fast/attn_prefill_tc.cuh"
 #include "fast/attn_prep.cuh"
+#include "fast/deltanet_step_batched.cuh"
 #include "kernels/attention_decode.hpp"
 #include "kernels/attention_prefill.hpp"
 #include "kernels/deltanet_chunk.hpp"
@@ -460,6 +461,35 @@ int miso_attn_prefill_tc(const miso_attn_prefill_tc_params* p, void* stream) {
   a.n_qtiles = (p->n + pf::kTokens - 1) / pf::kTokens;
   pf::prefill_kernel<<<2 * a.n_qtiles, pf::kThreads, pf::kSmemBytes, as_stream(stream)>>>(
       qmap, kmap, vmap, a);
+  return launch_status();
+}
+
+int miso_deltanet_step_batched(const miso_deltanet_step_batched_params* p, void* stream) {
+  if (p == nullptr || p->qkv == nullptr || p->z == nullptr || p->a == nullptr ||
+      p->b == nullptr || p->conv_w == nullptr || p->ssm_a == nullptr || p->dt_bias == nullptr ||
+      p->norm_w == nullptr || p->conv_in == nullptr || p->conv_out == nullptr ||
+      p->conv_in == p->conv_out || p->state == nullptr || p->out == nullptr || p->batch == 0 ||
+      p->batch > 65535 || !aligned16(p->state) || !aligned16(p->out) ||
+      !aligned16(p->norm_w))
+    return MISO_ERR_INVALID;
+  namespace ds = miso::fast::dnstep;
+  ds::Args a;
+  a.qkv = p->qkv;
+  a.z = p->z;
+  a.a = p->a;
+  a.b = p->b;
+  a.conv_w = p->conv_w;
+  a.ssm_a = p->ssm_a;
+  a.dt_bias = p->dt_bias;
+  a.norm_w = p->norm_w;
+  a.conv_in = p->conv_in;
+  a.conv_out = p->conv_out;
+  a.state = p->state;
+  a.out = p->out;
+  a.batch = p->batch;
+  a.in_stride = p->in_stride;
+  a.eps = p->eps;
+  ds::step_batched_kernel<<<dim3(ds::kVHeads, p->batch), ds::kThreads, 0, as_stream(stream)>>>(a);
   return launch_status();
 }
 

@@ -3,9 +3,9 @@
 // sm_100a device building blocks shared by the fast kernels: shared-memory addressing, mbarriers
 // with bounded waits, TMA tile loads, ldmatrix / movmatrix and the m16n8k16 f16 MMA.
 //
-// Every wait on an mbarrier is bounded by wall-clock time (%globaltimer). When a wait gives up, the
-// kernel records MISO_STATUS_TIMEOUT in the library's device status word and the caller returns
-// instead of spinning forever; the host reads the word with miso_device_status().
+// Every wait on an mbarrier is bounded (SM clock cycles). When a wait gives up, the kernel records
+// MISO_STATUS_TIMEOUT and the waiting site in the library's device status word and stops issuing
+// work instead of spinning forever; the host reads the word with miso_device_status().
 
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -19,22 +19,21 @@ namespace miso::dev {
 constexpr int kStatusOk = 0;
 constexpr int kStatusTimeout = 1;
 
-// Bound on any single mbarrier wait: 2 s of wall clock. Legitimate waits here are microseconds.
-constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+// Bound on any single mbarrier wait, in SM clock cycles (the per-SM cycle counter is monotonic):
+// 4e9 cycles, about 2 s at the B200's 1.9-2.0 GHz. Legitimate waits here are microseconds.
+constexpr long long kWaitLimitCycles = 4000000000ll;
 
 // Device status word of this library (one per device per loaded copy of the library).
 __device__ int g_status = 0;
 
-__device__ __forceinline__ void set_status(int code) { atomicCAS(&g_status, kStatusOk, code); }
+// Records the first failure of the process on this device: low byte = code, bits 8.. = the site
+// (which kernel and which wait) that hit it.
+__device__ __forceinline__ void set_status(int code, int site = 0) {
+  atomicCAS(&g_status, kStatusOk, code | (site << 8));
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ unsigned long long globaltimer() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
 }
 
 // ---- mbarrier -------------------------------------------------------------------------------
@@ -73,17 +72,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Waits for the phase with the given parity to complete. Returns false (and records a timeout in
-// the status word) if it has not completed within kWaitLimitNs.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+// Waits for the phase with the given parity to complete. Returns false (and records a timeout and
+// `site` in the status word) if it has not completed within kWaitLimitCycles.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int site = 0) {
   if (mbar_try_wait(bar, parity))
     return true;
-  const unsigned long long t0 = globaltimer();
+  const long long t0 = clock64();
   for (unsigned i = 1;; ++i) {
     if (mbar_try_wait(bar, parity))
       return true;
-    if ((i & 255u) == 0 && globaltimer() - t0 > kWaitLimitNs) {
-      set_status(kStatusTimeout);
+    if ((i & 255u) == 0 && clock64() - t0 > kWaitLimitCycles) {
+      set_status(kStatusTimeout, site);
       return false;
     }
   }

@@ -37,6 +37,7 @@ namespace miso::fast::decode {
 constexpr int kQHeads = 16, kKvHeads = 2, kDim = 256, kGroup = 8;
 constexpr int kTile = 64;                      // keys per pipeline stage
 constexpr int kStages = 3;
+constexpr int kBars = 6;  // lcm(kStages, 2)
 constexpr int kConsumerWarps = 8;
 constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kThreads = kConsumers + 32;      // + producer warp
@@ -66,7 +67,10 @@ struct Smem {
   float slot[2][kSlotFloats];
   float red_m[kConsumerWarps][kGroup];
   int seq_start[kMaxBatch + 1];
-  uint64_t full[kStages], empty[kStages];
+  // Barriers are indexed by tile % kBars (kBars = lcm(kStages, 2 warp groups)): every barrier is
+  // then used by one warp group only, in tile order, so a parity wait never has to tell a phase
+  // from the one two steps before it.
+  uint64_t full[kBars], empty[kBars];
   int abort_flag;
   int is_last;
 };
@@ -134,7 +138,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       sm.seq_start[a.batch] = incl;
   }
   if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < kBars; ++s) {
       dev::mbar_init(dev::smem_u32(&sm.full[s]), 1);
       dev::mbar_init(dev::smem_u32(&sm.empty[s]), 4);
     }
@@ -150,6 +154,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // ---------------------------------------------------------------------------------- producer
   if (warp == kConsumerWarps) {
     if (lane == 0 && t_begin < t_end) {
+      unsigned issued = 0;  // tiles whose loads have been issued
       dev::tma_prefetch_desc(&kmap);
       dev::tma_prefetch_desc(&vmap);
       const uint64_t policy = dev::policy_evict_first();
@@ -160,14 +165,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         const unsigned nt = (sm.seq_start[b + 1] - sm.seq_start[b]) / 2;
         const unsigned local = i - sm.seq_start[b], kvh = local / nt, j = local - kvh * nt;
         const int y = static_cast<int>(a.kv_row[2 * b + kvh] + int64_t(j) * kTile);
-        const unsigned k = i - t_begin, s = k % kStages, n = k / kStages;
-        const uint32_t full = dev::smem_u32(&sm.full[s]), empty = dev::smem_u32(&sm.empty[s]);
-        if (n > 0 && !dev::mbar_wait(empty, (n - 1) & 1)) {
+        const unsigned k = i - t_begin, s = k % kStages;
+        const uint32_t full = dev::smem_u32(&sm.full[k % kBars]);
+        // Stage s is free once tile k - kStages has been consumed (its group's empty barrier).
+        if (k >= kStages &&
+            !dev::mbar_wait(dev::smem_u32(&sm.empty[(k - kStages) % kBars]),
+                            ((k - kStages) / kBars) & 1, 0x11)) {
           sm.abort_flag = 1;
           break;
         }
         if (*reinterpret_cast<volatile int*>(&sm.abort_flag))
           break;
+        issued = k + 1;
         dev::mbar_arrive_expect_tx(full, kStageBytes);
         const uint32_t kdst = dev::smem_u32(stages + size_t(s) * kStageBytes);
         const uint32_t vdst = kdst + kHalfStage;
@@ -177,9 +186,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           dev::tma_load_2d_hint(vdst + box * kBoxBytes, &vmap, box * 64, y, full, policy);
         }
       }
+      if (*reinterpret_cast<volatile int*>(&sm.abort_flag)) {
+        // Let the copies of the last (up to kStages) issued tiles land before the CTA can exit.
+        for (unsigned k = issued > kStages ? issued - kStages : 0; k < issued; ++k)
+          dev::mbar_wait(dev::smem_u32(&sm.full[k % kBars]), (k / kBars) & 1, 0x13);
+      }
     }
-    return;
-  }
+    __syncwarp();  // the producer lane rejoins its warp before the block-wide barrier
+  } else {
 
   // ---------------------------------------------------------------------------------- consumers
   // Sequences with no keys produce zeros; CTA min(owner, P - 1) of their (empty) tile index
@@ -194,8 +208,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (unsigned i = tid; i < kQHeads * kDim; i += kConsumers)
       a.core[size_t(b) * kQHeads * kDim + i] = 0.0f;
   }
-  if (t_begin >= t_end)
-    return;
+  if (t_begin < t_end) {
 
   const unsigned group = warp / 4, slab = (warp % 4) * 16;
   const unsigned g = lane / 4, tq = lane % 4;  // fragment row group / thread-in-group
@@ -378,9 +391,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if ((k & 1) != group)
       continue;
     const unsigned s = k % kStages;
-    const uint32_t full = dev::smem_u32(&sm.full[s]);
+    const uint32_t full = dev::smem_u32(&sm.full[k % kBars]);
     bool ok = !*reinterpret_cast<volatile int*>(&sm.abort_flag);
-    if (ok && !dev::mbar_wait(full, (k / kStages) & 1)) {
+    if (ok && !dev::mbar_wait(full, (k / kBars) & 1, 0x12)) {
       sm.abort_flag = 1;
       ok = false;
     }
@@ -469,10 +482,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
     if (lane == 0)
-      dev::mbar_arrive(dev::smem_u32(&sm.empty[s]));
+      dev::mbar_arrive(dev::smem_u32(&sm.empty[k % kBars]));
   }
   if (cur_b != ~0u)
     finish(cur_b, cur_kvh);
+  }  // t_begin < t_end
+  }  // consumers
+  __syncthreads();  // no thread exits while copies into this CTA's shared memory may be pending
 }
 
 }  // namespace miso::fast::decode

@@ -88,7 +88,7 @@ __device__ __forceinline__ bool aborted(const Bars& b) {
 __device__ __forceinline__ bool wait_or_abort(Bars& b, uint64_t& bar, uint32_t parity) {
   if (aborted(b))
     return false;
-  if (!dev::mbar_wait(dev::smem_u32(&bar), parity)) {
+  if (!dev::mbar_wait(dev::smem_u32(&bar), parity, 0x20)) {
     b.abort_flag = 1;
     return false;
   }

@@ -47,6 +47,7 @@ def test_ctypes_structs_match_the_c_header():
         "miso_attn_decode_params": capi.AttnDecodeParams,
         "miso_attn_prep_batched_params": capi.AttnPrepBatchedParams,
         "miso_attn_prefill_tc_params": capi.AttnPrefillTcParams,
+        "miso_deltanet_step_batched_params": capi.DeltaNetStepBatchedParams,
     }
     lines = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{HEADER}"', "int main(){"]
     for cname, py in structs.items():
@@ -102,6 +103,8 @@ def test_invalid_arguments_are_rejected_without_a_device():
     assert lib.miso_deltanet_seq(None, None) == -1
     assert lib.miso_deltanet_chunk(None, None) == -1
     assert lib.miso_attn_prep_batched(None, None) == -1
+    assert lib.miso_deltanet_step_batched(None, None) == -1
+    assert lib.miso_attn_prefill_tc(None, None) == -1
     st = C.c_int(0)
     assert lib.miso_device_status(0, None) == -1
     assert st.value == 0
