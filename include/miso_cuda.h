@@ -322,6 +322,18 @@ typedef struct {
 
 int miso_deltanet_step_batched(const miso_deltanet_step_batched_params* p, void* stream);
 
+/* Gated DeltaNet prefill of n tokens on the tensor cores: the same inputs, outputs, conv history
+ * hand-off and in-place state update as miso_deltanet_seq (deltanet_seq_kernel,
+ * kernels/deltanet_step.hpp:146-273, launched at src/engine/deltanet.hip:112), computed with the
+ * chunked gated delta rule (chunk 64; kernels/deltanet_chunk.hpp:3-9) instead of token by token.
+ * Outputs agree with the recurrence to ~1e-4 relative (fp16 operands, fp32 accumulation and
+ * state). Requires conv_in != conv_out, qkv and state 16-byte aligned, qkv_stride a multiple of 4,
+ * and `scratch` (256-byte aligned) of at least miso_deltanet_prefill_tc_scratch_bytes(n) bytes,
+ * which the call overwrites. */
+size_t miso_deltanet_prefill_tc_scratch_bytes(unsigned n);
+int miso_deltanet_prefill_tc(const miso_deltanet_seq_params* p, void* scratch, size_t scratch_bytes,
+                             void* stream);
+
 /* ---------------------------------------------------------------------------------------------
  * Library state
  * ------------------------------------------------------------------------------------------- */

@@ -20,6 +20,7 @@
 #include "fast/attn_prefill_tc.cuh"
 #include "fast/attn_prep.cuh"
 #include "fast/deltanet_step_batched.cuh"
+#include "fast/deltanet_chunk_tc.cuh"
 #include "kernels/attention_decode.hpp"
 #include "kernels/attention_prefill.hpp"
 #include "kernels/deltanet_chunk.hpp"
@@ -115,6 +116,14 @@ int device_info(DeviceInfo** out) {
       a = cudaFuncSetAttribute(miso::fast::prefill::prefill_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(miso::fast::prefill::kSmemBytes));
+    if (a == cudaSuccess)
+      a = cudaFuncSetAttribute(miso::fast::dnchunk::prepare_kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(miso::fast::dnchunk::kPrepSmemBytes));
+    if (a == cudaSuccess)
+      a = cudaFuncSetAttribute(miso::fast::dnchunk::recur_kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(miso::fast::dnchunk::kRecurSmemBytes));
     d.status = a == cudaSuccess ? MISO_OK : static_cast<int>(a);
   });
   *out = &d;
@@ -490,6 +499,171 @@ int miso_deltanet_step_batched(const miso_deltanet_step_batched_params* p, void*
   a.in_stride = p->in_stride;
   a.eps = p->eps;
   ds::step_batched_kernel<<<dim3(ds::kVHeads, p->batch), ds::kThreads, 0, as_stream(stream)>>>(a);
+  return launch_status();
+}
+
+// Scratch of miso_deltanet_prefill_tc, each part 1024-byte aligned: q16, k16 [n][16][128] and
+// v16 [n][32][128] fp16 with their fp16 remainders, beta, log_a, e^g, e^(g_last - g) [32][np]
+// fp32, Tw, Tu, Aqk and its remainder [32][nc][64][64] fp16
+// (np = 64 nc, nc = ceil(n / 64)).
+struct DnChunkScratch {
+  size_t q16, k16, v16, q16lo, k16lo, v16lo, beta, loga, eg, egl, tw, tu, aqk, aqklo, total;
+};
+
+static DnChunkScratch dn_chunk_scratch(unsigned n) {
+  const size_t nc = (size_t(n) + 63) / 64, np = 64 * nc;
+  auto up = [](size_t x) { return (x + 1023) & ~size_t(1023); };
+  DnChunkScratch s;
+  size_t o = 0;
+  s.q16 = o, o += up(size_t(n) * 16 * 128 * 2);
+  s.k16 = o, o += up(size_t(n) * 16 * 128 * 2);
+  s.v16 = o, o += up(size_t(n) * 32 * 128 * 2);
+  s.q16lo = o, o += up(size_t(n) * 16 * 128 * 2);
+  s.k16lo = o, o += up(size_t(n) * 16 * 128 * 2);
+  s.v16lo = o, o += up(size_t(n) * 32 * 128 * 2);
+  s.beta = o, o += up(32 * np * 4);
+  s.loga = o, o += up(32 * np * 4);
+  s.eg = o, o += up(32 * np * 4);
+  s.egl = o, o += up(32 * np * 4);
+  s.tw = o, o += up(32 * nc * 64 * 64 * 2);
+  s.tu = o, o += up(32 * nc * 64 * 64 * 2);
+  s.aqk = o, o += up(32 * nc * 64 * 64 * 2);
+  s.aqklo = o, o += up(32 * nc * 64 * 64 * 2);
+  s.total = o;
+  return s;
+}
+
+size_t miso_deltanet_prefill_tc_scratch_bytes(unsigned n) {
+  return n == 0 ? 0 : dn_chunk_scratch(n).total;
+}
+
+int miso_deltanet_prefill_tc(const miso_deltanet_seq_params* p, void* scratch, size_t scratch_bytes,
+                             void* stream) {
+  namespace dc = miso::fast::dnchunk;
+  if (p == nullptr || p->qkv == nullptr || p->z == nullptr || p->a == nullptr ||
+      p->b == nullptr || p->conv_w == nullptr || p->conv_in == nullptr ||
+      p->conv_out == nullptr || p->conv_in == p->conv_out || p->ssm_a == nullptr ||
+      p->dt_bias == nullptr || p->norm_w == nullptr || p->state == nullptr ||
+      p->out == nullptr || p->n == 0 || p->n > (1u << 24) || p->qkv_stride % 4 != 0 ||
+      p->qkv_stride < 8192 || p->zab_stride < 4160 || !aligned16(p->qkv) ||
+      !aligned16(p->state) || !aligned16(p->conv_w) || scratch == nullptr ||
+      (reinterpret_cast<uintptr_t>(scratch) & 255u) != 0)
+    return MISO_ERR_INVALID;
+  const DnChunkScratch L = dn_chunk_scratch(p->n);
+  if (scratch_bytes < L.total)
+    return MISO_ERR_SCRATCH;
+  DeviceInfo* d = nullptr;
+  int st = device_info(&d);
+  if (st != MISO_OK)
+    return st;
+  if ((st = tensor_map_encoder()) != MISO_OK)
+    return st;
+  char* base = static_cast<char*>(scratch);
+  __half* q16 = reinterpret_cast<__half*>(base + L.q16);
+  __half* k16 = reinterpret_cast<__half*>(base + L.k16);
+  __half* v16 = reinterpret_cast<__half*>(base + L.v16);
+  __half* q16lo = reinterpret_cast<__half*>(base + L.q16lo);
+  __half* k16lo = reinterpret_cast<__half*>(base + L.k16lo);
+  __half* v16lo = reinterpret_cast<__half*>(base + L.v16lo);
+  float* beta = reinterpret_cast<float*>(base + L.beta);
+  float* loga = reinterpret_cast<float*>(base + L.loga);
+  float* eg = reinterpret_cast<float*>(base + L.eg);
+  float* egl = reinterpret_cast<float*>(base + L.egl);
+  __half* tw = reinterpret_cast<__half*>(base + L.tw);
+  __half* tu = reinterpret_cast<__half*>(base + L.tu);
+  __half* aqk = reinterpret_cast<__half*>(base + L.aqk);
+  __half* aqklo = reinterpret_cast<__half*>(base + L.aqklo);
+  const unsigned nc = (p->n + 63) / 64, np = 64 * nc;
+
+  CUtensorMap qmap, kmap, qlmap, klmap, vmap, vlmap, twmap, tumap, aqkmap, aqklmap;
+  {
+    const cuuint64_t dims[3] = {128, 16, p->n};
+    const cuuint64_t strides[2] = {128 * 2, 16 * 128 * 2};
+    const cuuint32_t box[3] = {64, 1, 64};
+    if ((st = f16_map(&qmap, q16, 3, dims, strides, box)) != MISO_OK ||
+        (st = f16_map(&kmap, k16, 3, dims, strides, box)) != MISO_OK ||
+        (st = f16_map(&qlmap, q16lo, 3, dims, strides, box)) != MISO_OK ||
+        (st = f16_map(&klmap, k16lo, 3, dims, strides, box)) != MISO_OK)
+      return st;
+  }
+  {
+    const cuuint64_t dims[3] = {128, 32, p->n};
+    const cuuint64_t strides[2] = {128 * 2, 32 * 128 * 2};
+    const cuuint32_t box[3] = {64, 1, 64};
+    if ((st = f16_map(&vmap, v16, 3, dims, strides, box)) != MISO_OK ||
+        (st = f16_map(&vlmap, v16lo, 3, dims, strides, box)) != MISO_OK)
+      return st;
+  }
+  {
+    const cuuint64_t dims[2] = {64, uint64_t(32) * nc * 64};
+    const cuuint64_t strides[1] = {64 * 2};
+    const cuuint32_t box[2] = {64, 64};
+    if ((st = f16_map(&twmap, tw, 2, dims, strides, box)) != MISO_OK ||
+        (st = f16_map(&tumap, tu, 2, dims, strides, box)) != MISO_OK ||
+        (st = f16_map(&aqkmap, aqk, 2, dims, strides, box)) != MISO_OK ||
+        (st = f16_map(&aqklmap, aqklo, 2, dims, strides, box)) != MISO_OK)
+      return st;
+  }
+  cudaStream_t s = as_stream(stream);
+
+  dc::ConvArgs ca;
+  ca.qkv = p->qkv;
+  ca.a = p->a;
+  ca.b = p->b;
+  ca.conv_w = p->conv_w;
+  ca.conv_in = p->conv_in;
+  ca.conv_out = p->conv_out;
+  ca.ssm_a = p->ssm_a;
+  ca.dt_bias = p->dt_bias;
+  ca.q16 = q16;
+  ca.k16 = k16;
+  ca.v16 = v16;
+  ca.q16lo = q16lo;
+  ca.k16lo = k16lo;
+  ca.v16lo = v16lo;
+  ca.beta = beta;
+  ca.loga = loga;
+  ca.n = p->n;
+  ca.np = np;
+  ca.qkv_stride = p->qkv_stride;
+  ca.zab_stride = p->zab_stride;
+  dc::conv_kernel<<<dim3(8, (p->n + dc::kConvTokens - 1) / dc::kConvTokens), dc::kConvThreads, 0,
+                    s>>>(ca);
+  if ((st = launch_status()) != MISO_OK)
+    return st;
+
+  dc::PrepareArgs pa;
+  pa.beta = beta;
+  pa.loga = loga;
+  pa.eg = eg;
+  pa.egl = egl;
+  pa.tw = tw;
+  pa.tu = tu;
+  pa.aqk = aqk;
+  pa.aqklo = aqklo;
+  pa.n = p->n;
+  pa.np = np;
+  pa.nc = nc;
+  dc::prepare_kernel<<<dim3(nc, 16), dc::kPrepThreads, dc::kPrepSmemBytes, s>>>(qmap, kmap, qlmap,
+                                                                                 klmap, pa);
+  if ((st = launch_status()) != MISO_OK)
+    return st;
+
+  dc::RecurArgs ra;
+  ra.eg = eg;
+  ra.egl = egl;
+  ra.z = p->z;
+  ra.norm_w = p->norm_w;
+  ra.state = p->state;
+  ra.out = p->out;
+  ra.n = p->n;
+  ra.np = np;
+  ra.nc = nc;
+  ra.zab_stride = p->zab_stride;
+  ra.z_prefetch = aligned16(p->z) && p->zab_stride % 4 == 0;
+  ra.eps = p->eps;
+  dc::recur_kernel<<<32, dc::kRecurThreads, dc::kRecurSmemBytes, s>>>(
+      qmap, kmap, vmap, vlmap, twmap, tumap, aqkmap, aqklmap, ra);
   return launch_status();
 }
 

@@ -105,6 +105,17 @@ def test_invalid_arguments_are_rejected_without_a_device():
     assert lib.miso_attn_prep_batched(None, None) == -1
     assert lib.miso_deltanet_step_batched(None, None) == -1
     assert lib.miso_attn_prefill_tc(None, None) == -1
+    assert lib.miso_deltanet_prefill_tc(None, None, 0, None) == -1
+    assert lib.miso_deltanet_prefill_tc_scratch_bytes(0) == 0
+    sb = lib.miso_deltanet_prefill_tc_scratch_bytes(8192)
+    assert sb >= 8192 * 16384 + 3 * 32 * 128 * 8192  # fp16 q/k/v and the three chunk tiles
+    # conv_in == conv_out and a short scratch are refused before any device work.
+    fake = 1 << 20
+    dp = capi.DeltaNetSeqParams(fake, fake, fake, fake, fake, fake, fake, fake, fake, fake, fake,
+                                fake, 64, 1e-6, 4160, 8192)
+    assert lib.miso_deltanet_prefill_tc(C.byref(dp), fake, 1 << 30, None) == -1
+    dp.conv_out = fake * 2
+    assert lib.miso_deltanet_prefill_tc(C.byref(dp), fake, 1024, None) == -2
     st = C.c_int(0)
     assert lib.miso_device_status(0, None) == -1
     assert st.value == 0
