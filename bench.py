@@ -301,6 +301,9 @@ def run_miso(args) -> None:
                                                          barrier, world)
     dn_step = None if args.no_deltanet else bench_deltanet_step(args, dev, stream,
                                                                 max_over_ranks, barrier, world)
+    dn_prefill = None if args.no_deltanet else bench_deltanet_prefill(args, dev, stream,
+                                                                      max_over_ranks, barrier,
+                                                                      world)
 
     st = ctypes.c_int(-1)
     capi.check("miso_device_status", capi.load().miso_device_status(1, st))
@@ -351,6 +354,7 @@ def run_miso(args) -> None:
         "cpu_baseline": cpu,
         "prefill": prefill,
         "deltanet_step": dn_step,
+        "deltanet_prefill": dn_prefill,
     }
     print(json.dumps(line), flush=True)
 
@@ -495,6 +499,80 @@ def bench_deltanet_step(args, dev, stream, max_over_ranks, barrier, world) -> di
                          "kernel": "step_batched_kernel", "kernel_ms": ms,
                          "peak_source": pk["source"]},
             "gpu_launches": args.steps}
+
+
+DN_PREFILL_T = 8192
+# Algorithmic FLOPs of the chunked rule per (V head, chunk of 64): 2 (3 C d^2 + 3 C^2 d)
+# = 9.44 MFLOP (QK^T / KK^T, the UT-transform products, S updates), 32 heads x T / 64 chunks.
+DN_PREFILL_FLOPS_PER_HEAD_CHUNK = 2.0 * (3 * 64 * 128 * 128 + 3 * 64 * 64 * 128)
+
+
+def bench_deltanet_prefill(args, dev, stream, max_over_ranks, barrier, world) -> dict:
+    """BASELINE config 4a: Gated DeltaNet chunked prefill of T = 8192 tokens per GPU (one
+    sequence per rank), bf16-valued N(0,1) projections, conv_w N(0, 0.5), ssm_a = -1,
+    dt_bias = 0, zero initial state and conv history; one step = miso_deltanet_prefill_tc (conv +
+    norms, per-chunk UT transform, state recurrence with the gated RMS-norm output)."""
+    import torch
+    from miso_b200 import capi
+
+    T = DN_PREFILL_T
+    g = torch.Generator(device=dev)
+    g.manual_seed(1)
+    proj = torch.randn((T, DN_PROJ), generator=g, device=dev).bfloat16().float()
+    conv_w = (0.5 * torch.randn((8192, 4), generator=g, device=dev)).bfloat16().float()
+    ssm_a = -torch.ones(32, device=dev)
+    dt = torch.zeros(32, device=dev)
+    norm_w = torch.ones(128, device=dev)
+    conv = [torch.zeros((8192, 3), device=dev) for _ in range(2)]
+    state = torch.zeros((32, 128, 128), device=dev)
+    out = torch.empty((T, 4096), device=dev)
+    lib = capi.load()
+    sb = lib.miso_deltanet_prefill_tc_scratch_bytes(T)
+    scratch = torch.empty(sb, dtype=torch.uint8, device=dev)
+    base = proj.data_ptr()
+    z = base + 8192 * 4
+    params = [capi.DeltaNetSeqParams(base, z, z + 4096 * 4, z + 4128 * 4, conv_w.data_ptr(),
+                                     conv[i].data_ptr(), conv[1 - i].data_ptr(), ssm_a.data_ptr(),
+                                     dt.data_ptr(), norm_w.data_ptr(), state.data_ptr(),
+                                     out.data_ptr(), T, EPS, DN_PROJ, DN_PROJ)
+              for i in range(2)]
+
+    def step(i):
+        capi.check("dn_prefill", lib.miso_deltanet_prefill_tc(
+            ctypes.byref(params[i % 2]), scratch.data_ptr(), sb, stream.cuda_stream))
+
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            step(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    flops = 32 * (T // 64) * DN_PREFILL_FLOPS_PER_HEAD_CHUNK
+    nbytes = T * (8192 + 4096 + 64) * 4 + T * 4096 * 4 + 2 * 32 * 128 * 128 * 4
+    pk = peaks()
+    tflops = flops / (ms * 1e-3) / 1e12
+    return {"metric": "DeltaNet chunked prefill tok/s @8192", "value": world * T / (ms * 1e-3),
+            "unit": "tokens/s", "ms_per_step": ms, "n_tokens": T,
+            "config": "BASELINE config 4a: 1 x 8192 tokens per GPU, 16 K / 32 V heads, d 128, "
+                      "chunk 64, bf16-valued inputs, zero initial state; fp16 hi/lo tensor "
+                      "operands, fp32 accumulation and state; 3 launches per step",
+            "flops_per_step": flops, "tflops": tflops, "bytes_per_step": nbytes,
+            "gbs": nbytes / (ms * 1e-3) / 1e9,
+            "roofline": {"bound": "tensor", "achieved": tflops, "peak": pk["bf16_tflops"],
+                         "unit": "TFLOP/s", "frac": tflops / pk["bf16_tflops"], "traffic": None,
+                         "kernel": "conv_kernel + prepare_kernel + recur_kernel", "kernel_ms": ms,
+                         "peak_source": pk["source"],
+                         "note": "latency-bound: the state recurrence is sequential over the "
+                                 "128 chunks of each of the 32 heads"},
+            "gpu_launches": 3 * args.steps}
 
 
 def main():

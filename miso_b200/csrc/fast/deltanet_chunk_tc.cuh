@@ -206,6 +206,8 @@ struct PrepareArgs {
 
 constexpr int kPrepThreads = 128;
 constexpr int kLRow = 68;  // fp32 row stride of L (16-byte aligned rows)
+constexpr int kTRow = 65;  // fp32 stride of a solved column of T (conflict-free per lane)
+static_assert((2 * 64 * kTRow + 4 * 64) * 4 <= 8 * 8192, "T columns fit in the [K; Q] tile area");
 // [K; Q] as fp16 high parts (32 KB) then remainders (32 KB): 64-dim slab s of part p at
 // 32 KB p + 16 KB s, K rows first, Q rows 8 KB later (M = 128 rows).
 constexpr uint32_t kPrepOffL = 8 * kTile;
@@ -356,32 +358,61 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
   }
   dev::tc_fence_before();
   __syncthreads();
+  // T = (I + L)^-1 by forward substitution, thread (hh, col) solving column col of V head
+  // kh + 16 hh: t_i = [i == col] - sum_{j<i} L_ij t_j. Rows go in blocks of 16: first the
+  // contributions of all earlier rows to the block's 16 rows (16 independent accumulators), then
+  // the block's own 16 x 16 triangle. Solved columns live in shared memory (Tc, in the [K; Q]
+  // tile area, free once the MMA has completed), which keeps the code compact.
+  float* Tc = reinterpret_cast<float*>(smem);  // [2][64 cols][kTRow]
+  float* fac = Tc + 2 * kC * kTRow;            // [2][2][64]: beta e^g (Tw), beta (Tu) per column
   if (ok) {
-    // Column col of T = (I + L)^-1 for V head kh + 16 hh: t_i = [i == col] - sum_{j<i} L_ij t_j.
-    const unsigned hh = tid / kC, col = tid % kC, h = kh + kKHeads * hh;
+    const unsigned hh = tid / kC, col = tid % kC;
     const float* L = Ls + hh * kC * kLRow;
-    float tc[kC];
+    float* tcol = Tc + (hh * kC + col) * kTRow;
+    const float bc = bs[hh * kC + col];
+    fac[(hh * 2 + 0) * kC + col] = bc * __expf(gs[hh * kC + col]);
+    fac[(hh * 2 + 1) * kC + col] = bc;
+#pragma unroll 1
+    for (int b = 0; b < kC / 16; ++b) {
+      const int i0 = 16 * b;
+      float acc[16];
 #pragma unroll
-    for (int i = 0; i < kC; ++i) {
-      float acc = i == int(col) ? 1.0f : 0.0f;
+      for (int r = 0; r < 16; ++r)
+        acc[r] = i0 + r == int(col) ? 1.0f : 0.0f;
+#pragma unroll 1
+      for (int j = 0; j < i0; j += 4) {
+        const float t0 = tcol[j], t1 = tcol[j + 1], t2 = tcol[j + 2], t3 = tcol[j + 3];
 #pragma unroll
-      for (int j4 = 0; j4 < i / 4; ++j4) {
-        const float4 l4 = *reinterpret_cast<const float4*>(L + i * kLRow + 4 * j4);
-        acc -= l4.x * tc[4 * j4] + l4.y * tc[4 * j4 + 1] + l4.z * tc[4 * j4 + 2] +
-               l4.w * tc[4 * j4 + 3];
+        for (int r = 0; r < 16; ++r) {
+          const float4 l4 = *reinterpret_cast<const float4*>(L + (i0 + r) * kLRow + j);
+          acc[r] -= l4.x * t0 + l4.y * t1 + l4.z * t2 + l4.w * t3;
+        }
       }
 #pragma unroll
-      for (int j = (i / 4) * 4; j < i; ++j)
-        acc -= L[i * kLRow + j] * tc[j];
-      tc[i] = acc;
-    }
-    const float bc = bs[hh * kC + col], ec = bc * __expf(gs[hh * kC + col]);
-    __half* tw = a.tw + (size_t(h) * a.nc + c) * kC * kC + col;
-    __half* tu = a.tu + (size_t(h) * a.nc + c) * kC * kC + col;
+      for (int r = 1; r < 16; ++r)
 #pragma unroll
-    for (int i = 0; i < kC; ++i) {
-      tw[i * kC] = __float2half_rn(tc[i] * ec);
-      tu[i * kC] = __float2half_rn(tc[i] * bc);
+        for (int q = 0; q < r; ++q)
+          acc[r] -= L[(i0 + r) * kLRow + i0 + q] * acc[q];
+#pragma unroll
+      for (int r = 0; r < 16; ++r)
+        tcol[i0 + r] = acc[r];
+    }
+  }
+  __syncthreads();
+  if (ok) {
+    // Tw = T diag(beta e^g), Tu = T diag(beta) as fp16 rows: 16-byte chunk (hh, which, i, k)
+    // holds columns 8k .. 8k + 7 of row i.
+    for (unsigned u = tid; u < 2 * 2 * kC * 8; u += kPrepThreads) {
+      const unsigned k = u % 8, i = (u / 8) % kC, which = (u / (8 * kC)) % 2, hh = u / (16 * kC);
+      const float* f = fac + (hh * 2 + which) * kC + 8 * k;
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        v[e] = Tc[(hh * kC + 8 * k + e) * kTRow + i] * f[e];
+      const unsigned h = kh + kKHeads * hh;
+      __half* dst = (which ? a.tu : a.tw) + ((size_t(h) * a.nc + c) * kC + i) * kC + 8 * k;
+      *reinterpret_cast<uint4*>(dst) =
+          make_uint4(h2(v[0], v[1]), h2(v[2], v[3]), h2(v[4], v[5]), h2(v[6], v[7]));
     }
   }
   if (tid == 0 && *reinterpret_cast<volatile int*>(fail))
