@@ -304,6 +304,8 @@ def run_miso(args) -> None:
     dn_prefill = None if args.no_deltanet else bench_deltanet_prefill(args, dev, stream,
                                                                       max_over_ranks, barrier,
                                                                       world)
+    cp_block = None if args.no_cp else bench_cp_block(args, dev, stream, max_over_ranks,
+                                                      barrier, world, rank)
 
     st = ctypes.c_int(-1)
     capi.check("miso_device_status", capi.load().miso_device_status(1, st))
@@ -355,6 +357,7 @@ def run_miso(args) -> None:
         "prefill": prefill,
         "deltanet_step": dn_step,
         "deltanet_prefill": dn_prefill,
+        "cp_block": cp_block,
     }
     print(json.dumps(line), flush=True)
 
@@ -575,6 +578,78 @@ def bench_deltanet_prefill(args, dev, stream, max_over_ranks, barrier, world) ->
             "gpu_launches": 3 * args.steps}
 
 
+CP_T = 131072
+CP_DN_LAYERS = 3
+
+
+def bench_cp_block(args, dev, stream, max_over_ranks, barrier, world, rank) -> dict:
+    """BASELINE config 5 (prefill part): one hybrid block (3 Gated DeltaNet + 1 gated GQA layer,
+    independent seeded bf16-valued N(0,1) mixer inputs, no projections) over one sequence of
+    T = 131072 tokens, context-parallel over the ranks: attention with zig-zag chunks and the KV
+    all-gather, DeltaNet with the state hand-off wavefront (miso_b200.cp). At one GPU the same
+    code runs the whole sequence locally. Step = the block's prefill; tokens/s = T / step."""
+    import torch
+    from miso_b200 import attention as A
+    from miso_b200 import cp
+
+    t = args.cp_t
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    proj = torch.randn((t, cp.ATTN_PROJ), generator=g, device=dev).bfloat16().float()
+    projs = [torch.randn((t, cp.DN_PROJ), generator=g, device=dev).bfloat16().float()
+             for _ in range(CP_DN_LAYERS)]
+    ones = torch.ones(DIM, device=dev)
+    inv = torch.from_numpy(A.rope_inv_freq()).to(dev)
+    conv_w = (0.5 * torch.randn((8192, 4), generator=g, device=dev)).bfloat16().float()
+    ssm_a, dt = -torch.ones(32, device=dev), torch.zeros(32, device=dev)
+    norm_w = torch.ones(128, device=dev)
+    attn = cp.GpuAttentionCp(t, world, rank, proj, ones, ones, inv, EPS, stream)
+    dn = cp.GpuDeltaNetWavefront(t, world, rank, projs, conv_w, ssm_a, dt, norm_w, EPS, stream)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+
+    def step(record=False):
+        if record:
+            ev[0].record(stream)
+        attn.run()
+        if record:
+            ev[1].record(stream)
+        dn.run()
+        if record:
+            ev[2].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    attn_ms = dn_ms = tot_ms = 0.0
+    for _ in range(args.cp_steps):
+        barrier()
+        torch.cuda.synchronize()
+        step(record=True)
+        torch.cuda.synchronize()
+        barrier()
+        attn_ms += max_over_ranks(ev[0].elapsed_time(ev[1]))
+        dn_ms += max_over_ranks(ev[1].elapsed_time(ev[2]))
+        tot_ms += max_over_ranks(ev[0].elapsed_time(ev[2]))
+    k = args.cp_steps
+    attn_ms, dn_ms, tot_ms = attn_ms / k, dn_ms / k, tot_ms / k
+    a_flops = 8192.0 * t * (t + 1)
+    d_flops = CP_DN_LAYERS * 32 * (t // 64) * DN_PREFILL_FLOPS_PER_HEAD_CHUNK
+    pk = peaks()
+    a_tf = a_flops / (attn_ms * 1e-3) / 1e12
+    return {"metric": f"hybrid block prefill tok/s @{t}", "value": t / (tot_ms * 1e-3),
+            "unit": "tokens/s", "ms_per_step": tot_ms, "steps": k, "n_tokens": t,
+            "scaling": "strong",
+            "config": "BASELINE config 5 prefill: 1 x 131072 tokens over the ranks; 1 gated GQA "
+                      "layer (config 3 shapes) context-parallel with zig-zag chunks and an NCCL "
+                      "KV all-gather; 3 Gated DeltaNet layers (config 4 shapes) as a state "
+                      "hand-off wavefront over contiguous segments",
+            "attention": {"ms": attn_ms, "tflops_per_gpu": a_tf / world, "flops": a_flops,
+                          "frac_of_peak_per_gpu": a_tf / world / pk["bf16_tflops"]},
+            "deltanet": {"ms": dn_ms, "flops": d_flops, "layers": CP_DN_LAYERS},
+            "gpu_launches": k * (4 + 3 * CP_DN_LAYERS)}
+
+
 def main():
     global BATCH
     ap = argparse.ArgumentParser()
@@ -593,6 +668,11 @@ def main():
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="sequences per GPU (default 32, the BASELINE config; smaller only for "
                          "profiling captures)")
+    ap.add_argument("--cp-t", type=int, default=CP_T,
+                    help="tokens of the context-parallel hybrid block (BASELINE config 5)")
+    ap.add_argument("--cp-steps", type=int, default=3,
+                    help="timed steps of the config 5 block (each is a 131072-token prefill)")
+    ap.add_argument("--no-cp", action="store_true", help="skip the config 5 block")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

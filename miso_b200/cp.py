@@ -1,0 +1,236 @@
+"""Context-parallel prefill of one long sequence over the ranks of one node (one process per GPU).
+
+Attention (the gated GQA layer): zig-zag partition of the T tokens into 2W chunks of T / 2W; rank
+r owns chunks r and 2W - 1 - r, which balances the causal work (chunk i costs ~ i + 1/2). Each
+rank runs the prep (norms, RoPE, fp16 KV append) of its own tokens into a full-length KV cache,
+the ranks exchange their KV chunks (the only collective of the attention layer; every rank ends
+up holding the whole cache, which the decode phase then reuses), and each rank runs the causal
+tensor-core prefill of its two query chunks against all keys before them
+(miso_attn_prefill_tc with pos0 = chunk start).
+
+Gated DeltaNet layers: the recurrence needs the state at the end of the previous tokens, so the
+sequence is cut into W contiguous segments and the state (with the conv history) is handed from
+rank r - 1 to rank r. Independent layers form a wavefront: rank r runs layer l while rank r + 1
+runs layer l - 1, so L layers take (W + L - 1) segment times instead of W L.
+
+The orchestration is written against small callables (compute a segment, send / receive a state,
+all-gather a chunk) so that the same code runs over NCCL with the CUDA kernels and over gloo with
+the CPU oracle in the tests.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable, Sequence
+
+
+def zigzag_chunks(t: int, world: int, rank: int) -> list[tuple[int, int]]:
+    """(start, length) of the two chunks rank `rank` owns; t must be a multiple of 2 * world."""
+    if world < 1 or not 0 <= rank < world or t % (2 * world):
+        raise ValueError(f"zig-zag partition needs t % (2 * world) == 0 (t={t}, world={world})")
+    s = t // (2 * world)
+    return [(rank * s, s), ((2 * world - 1 - rank) * s, s)]
+
+
+def chunk_owner(t: int, world: int, chunk: int) -> int:
+    """Rank owning zig-zag chunk `chunk` (0 <= chunk < 2 world)."""
+    return chunk if chunk < world else 2 * world - 1 - chunk
+
+
+def causal_work(chunks: Sequence[tuple[int, int]]) -> int:
+    """Query-key pairs (key <= query) of the given query chunks: the attention work of a rank."""
+    return sum(n * start + n * (n + 1) // 2 for start, n in chunks)
+
+
+def contiguous_segment(t: int, world: int, rank: int) -> tuple[int, int]:
+    """(start, length) of rank's contiguous DeltaNet segment (the last rank takes the remainder)."""
+    s = t // world
+    return (rank * s, t - rank * s if rank == world - 1 else s)
+
+
+@dataclass
+class AttentionCp:
+    """One rank's share of the context-parallel attention prefill.
+
+    prep(start, n)        prep of tokens [start, start + n) into the local full-length cache
+    gather(chunk_index)   makes zig-zag chunk `chunk_index` of every rank present in the local
+                          cache (all-gather of that chunk's K / V over the ranks)
+    attend(start, n)      causal prefill of query tokens [start, start + n) against keys [0, start + n)
+    """
+    t: int
+    world: int
+    rank: int
+    prep: Callable[[int, int], None]
+    gather: Callable[[int], None]
+    attend: Callable[[int, int], None]
+
+    def run(self) -> None:
+        mine = zigzag_chunks(self.t, self.world, self.rank)
+        for start, n in mine:
+            self.prep(start, n)
+        # Chunk slot 0 (positions r s) and slot 1 (positions (2W - 1 - r) s) of every rank; every
+        # rank takes part in both all-gathers in the same order.
+        for slot in range(2):
+            self.gather(slot)
+        for start, n in mine:
+            self.attend(start, n)
+
+
+@dataclass
+class DeltaNetWavefront:
+    """One rank's share of L independent Gated DeltaNet layers over a sequence cut into W
+    contiguous segments.
+
+    run(layer, start, n)   prefill of tokens [start, start + n) of `layer` on the local state
+    reset(layer)           zero state and conv history (rank 0, the start of the sequence)
+    recv(layer)            receive layer's state and conv history from rank - 1
+    send(layer)            send them to rank + 1
+    """
+    t: int
+    world: int
+    rank: int
+    layers: int
+    run_segment: Callable[[int, int, int], None]
+    reset: Callable[[int], None]
+    recv: Callable[[int], None]
+    send: Callable[[int], None]
+
+    def run(self) -> None:
+        start, n = contiguous_segment(self.t, self.world, self.rank)
+        for layer in range(self.layers):
+            if self.rank == 0:
+                self.reset(layer)
+            else:
+                self.recv(layer)
+            self.run_segment(layer, start, n)
+            if self.rank + 1 < self.world:
+                self.send(layer)
+
+
+# ---- CUDA / NCCL bindings ----------------------------------------------------------------------
+
+ATTN_PROJ = 9216   # [q + gate 8192 | k 512 | v 512] per token
+DN_PROJ = 12352    # [qkv 8192 | z 4096 | a 32 | b 32] per token
+
+
+class GpuAttentionCp:
+    """Buffers and kernels of one rank's context-parallel attention prefill over a projection
+    buffer proj [t][9216] (the rank reads only its own rows). After run(), self.k / self.v hold
+    the whole [2][t][256] fp16 cache on every rank and self.core [t][16][256] the rank's rows."""
+
+    def __init__(self, t: int, world: int, rank: int, proj, q_norm, k_norm, inv_freq,
+                 eps: float, stream, group=None):
+        import torch
+        from . import _capi as capi
+        self.t, self.world, self.rank, self.group = t, world, rank, group
+        self.capi, self.lib = capi, capi.load()
+        dev = proj.device
+        self.proj, self.stream, self.eps = proj, stream, eps
+        self.norms = (q_norm, k_norm, inv_freq)
+        self.k = torch.zeros((2, t, 256), dtype=torch.float16, device=dev)
+        self.v = torch.zeros_like(self.k)
+        self.q16 = torch.empty((t, 16, 256), dtype=torch.float16, device=dev)
+        self.core = torch.empty((t, 16, 256), dtype=torch.float32, device=dev)
+        self.cp = AttentionCp(t, world, rank, self._prep, self._gather, self._attend)
+
+    def _prep(self, start: int, n: int) -> None:
+        import ctypes
+        capi = self.capi
+        qn, kn, inv = self.norms
+        base = self.proj.data_ptr() + start * ATTN_PROJ * 4
+        tok0 = capi.AttnPrepParams(base, base + 8192 * 4, base + 8704 * 4, qn.data_ptr(),
+                                   kn.data_ptr(), inv.data_ptr(), self.k.data_ptr(),
+                                   self.v.data_ptr(), 0, start, self.t, self.eps)
+        bp = capi.AttnPrepBatchParams(tok0, n, ATTN_PROJ)
+        capi.check("miso_attn_prep_batch_f16", self.lib.miso_attn_prep_batch_f16(
+            ctypes.byref(bp), self.q16.data_ptr() + start * 16 * 256 * 2, self.stream.cuda_stream))
+
+    def _gather(self, slot: int) -> None:
+        import torch.distributed as dist
+        if self.world == 1:
+            return
+        starts = [zigzag_chunks(self.t, self.world, r)[slot][0] for r in range(self.world)]
+        s = self.t // (2 * self.world)
+        mine = starts[self.rank]
+        for cache in (self.k, self.v):
+            for h in range(2):
+                dist.all_gather([cache[h, st:st + s] for st in starts], cache[h, mine:mine + s],
+                                group=self.group)
+
+    def _attend(self, start: int, n: int) -> None:
+        import ctypes
+        capi = self.capi
+        base = self.proj.data_ptr() + start * ATTN_PROJ * 4
+        tp = capi.AttnPrefillTcParams(self.q16.data_ptr() + start * 16 * 256 * 2, base,
+                                      self.k.data_ptr(), self.v.data_ptr(),
+                                      self.core.data_ptr() + start * 16 * 256 * 4, start, n,
+                                      self.t, ATTN_PROJ)
+        capi.check("miso_attn_prefill_tc", self.lib.miso_attn_prefill_tc(ctypes.byref(tp),
+                                                                         self.stream.cuda_stream))
+
+    def run(self) -> None:
+        import torch
+        with torch.cuda.stream(self.stream):
+            self.cp.run()
+
+
+class GpuDeltaNetWavefront:
+    """Buffers and kernels of one rank's share of L independent DeltaNet layers over projection
+    buffers projs[l] [t][12352]: the rank runs miso_deltanet_prefill_tc on its contiguous segment
+    with the state and conv history received from rank - 1 and passes them on to rank + 1.
+    After run(), self.state[l] / self.conv[l] hold the layer's state after the rank's segment
+    (the final state of the sequence on the last rank) and self.out[l] [t][4096] its rows."""
+
+    def __init__(self, t: int, world: int, rank: int, projs, conv_w, ssm_a, dt_bias, norm_w,
+                 eps: float, stream, group=None):
+        import torch
+        from . import _capi as capi
+        self.t, self.world, self.rank, self.group = t, world, rank, group
+        self.capi, self.lib = capi, capi.load()
+        dev = projs[0].device
+        self.projs, self.stream, self.eps = projs, stream, eps
+        self.w = (conv_w, ssm_a, dt_bias, norm_w)
+        L = len(projs)
+        self.state = [torch.zeros((32, 128, 128), device=dev) for _ in range(L)]
+        self.conv = [torch.zeros((8192, 3), device=dev) for _ in range(L)]
+        self.conv_out = [torch.zeros((8192, 3), device=dev) for _ in range(L)]
+        self.out = [torch.empty((t, 4096), device=dev) for _ in range(L)]
+        _, n = contiguous_segment(t, world, rank)
+        self.sb = self.lib.miso_deltanet_prefill_tc_scratch_bytes(n)
+        self.scratch = torch.empty(self.sb, dtype=torch.uint8, device=dev)
+        self.wf = DeltaNetWavefront(t, world, rank, L, self._run, self._reset, self._recv,
+                                    self._send)
+
+    def _run(self, layer: int, start: int, n: int) -> None:
+        import ctypes
+        capi = self.capi
+        conv_w, ssm_a, dt, norm_w = self.w
+        base = self.projs[layer].data_ptr() + start * DN_PROJ * 4
+        z = base + 8192 * 4
+        p = capi.DeltaNetSeqParams(base, z, z + 4096 * 4, z + 4128 * 4, conv_w.data_ptr(),
+                                   self.conv[layer].data_ptr(), self.conv_out[layer].data_ptr(),
+                                   ssm_a.data_ptr(), dt.data_ptr(), norm_w.data_ptr(),
+                                   self.state[layer].data_ptr(),
+                                   self.out[layer].data_ptr() + start * 4096 * 4, n, self.eps,
+                                   DN_PROJ, DN_PROJ)
+        capi.check("miso_deltanet_prefill_tc", self.lib.miso_deltanet_prefill_tc(
+            ctypes.byref(p), self.scratch.data_ptr(), self.sb, self.stream.cuda_stream))
+        self.conv[layer], self.conv_out[layer] = self.conv_out[layer], self.conv[layer]
+
+    def _reset(self, layer: int) -> None:
+        self.state[layer].zero_()
+        self.conv[layer].zero_()
+
+    def _recv(self, layer: int) -> None:
+        import torch.distributed as dist
+        dist.recv(self.state[layer], self.rank - 1, group=self.group)
+        dist.recv(self.conv[layer], self.rank - 1, group=self.group)
+
+    def _send(self, layer: int) -> None:
+        import torch.distributed as dist
+        dist.send(self.state[layer], self.rank + 1, group=self.group)
+        dist.send(self.conv[layer], self.rank + 1, group=self.group)
+
+    def run(self) -> None:
+        import torch
+        with torch.cuda.stream(self.stream):
+            self.wf.run()

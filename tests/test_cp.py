@@ -1,0 +1,72 @@
+"""Context-parallel prefill (miso_b200.cp): the partition arithmetic, and the multi-rank
+orchestration run as gloo ranks on the CPU with the oracle in place of the kernels (attention:
+zig-zag chunks + KV all-gather; DeltaNet: state hand-off wavefront), bit-exact against a
+single-process run."""
+import os
+import socket
+import subprocess
+import sys
+
+import pytest
+
+from miso_b200 import cp
+
+WORKER = os.path.join(os.path.dirname(os.path.abspath(__file__)), "support", "cp_worker.py")
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_zigzag_partition_covers_and_balances(world):
+    t = 2 * world * 1024
+    seen = []
+    for r in range(world):
+        for start, n in cp.zigzag_chunks(t, world, r):
+            seen.extend(range(start, start + n))
+            assert cp.chunk_owner(t, world, start // n) == r
+    assert sorted(seen) == list(range(t))
+    work = [cp.causal_work(cp.zigzag_chunks(t, world, r)) for r in range(world)]
+    assert max(work) / min(work) < 1.001
+    with pytest.raises(ValueError):
+        cp.zigzag_chunks(t + 1, world, 0)
+
+
+@pytest.mark.parametrize("world", [1, 3, 8])
+def test_contiguous_segments_cover(world):
+    t = 1000
+    segs = [cp.contiguous_segment(t, world, r) for r in range(world)]
+    assert segs[0][0] == 0 and sum(n for _, n in segs) == t
+    assert all(a[0] + a[1] == b[0] for a, b in zip(segs, segs[1:]))
+
+
+def free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def run_ranks(case: str, world: int) -> None:
+    port = free_port()
+    env = dict(os.environ, OMP_NUM_THREADS="1")
+    procs = [subprocess.Popen([sys.executable, WORKER, "--case", case, "--rank", str(r),
+                               "--world", str(world), "--port", str(port)], env=env,
+                              stdout=subprocess.PIPE, stderr=subprocess.STDOUT)
+             for r in range(world)]
+    outs = []
+    try:
+        for p in procs:
+            outs.append(p.communicate(timeout=240)[0].decode(errors="replace"))
+    finally:
+        for p in procs:
+            if p.poll() is None:
+                p.kill()
+    for r, (p, o) in enumerate(zip(procs, outs)):
+        assert p.returncode == 0, f"rank {r} of {case} (world {world}) failed:\n{o[-3000:]}"
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_attention_context_parallel_gloo(world):
+    run_ranks("attention", world)
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_deltanet_wavefront_gloo(world):
+    run_ranks("deltanet", world)
