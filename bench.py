@@ -580,6 +580,104 @@ def bench_deltanet_prefill(args, dev, stream, max_over_ranks, barrier, world) ->
 
 CP_T = 131072
 CP_DN_LAYERS = 3
+CP_DEC_BATCH = 8
+CP_DEC_STEPS = 256
+
+
+def cp_block_decode(args, dev, stream, max_over_ranks, barrier, world, rank, attn, dn, dn_group,
+                    g) -> dict:
+    """BASELINE config 5 (decode part): 256 decode steps of the block at a total batch of 8
+    sequences that continue from the context-parallel prefix. The 8 sequences are split over the
+    ranks; each rank already holds the whole prefix KV cache (from the prefill's all-gather) and
+    receives the DeltaNet states at the end of the prefix from the last rank (a broadcast). Step
+    = batched attention prep + split-K decode, then the batched DeltaNet step of each layer."""
+    import torch
+    import torch.distributed as dist
+    from miso_b200 import _capi as capi
+    from miso_b200 import attention as A
+
+    t, steps = attn.t, args.cp_decode_steps
+    nb = CP_DEC_BATCH // world + (1 if rank < CP_DEC_BATCH % world else 0)
+    if world > 1:
+        for layer in range(CP_DN_LAYERS):
+            dist.broadcast(dn.state[layer], world - 1, group=dn_group)
+            dist.broadcast(dn.conv[layer], world - 1, group=dn_group)
+    torch.cuda.synchronize()
+    if nb == 0:  # take part in the same collectives as the ranks that decode
+        barrier()
+        barrier()
+        max_over_ranks(0.0)
+        barrier()
+        return None
+    lib = capi.load()
+    cap = t + steps + args.warmup + 8
+    rows = nb * KV_HEADS * cap
+    pk_, pv_ = (torch.empty((rows, DIM), dtype=torch.float16, device=dev) for _ in range(2))
+    kv_row = torch.arange(nb * KV_HEADS, dtype=torch.int64, device=dev).reshape(nb, KV_HEADS) * cap
+    for b in range(nb):
+        for h in range(KV_HEADS):
+            r0 = (b * KV_HEADS + h) * cap
+            pk_[r0:r0 + t] = attn.k[h]
+            pv_[r0:r0 + t] = attn.v[h]
+    lens = torch.full((nb,), t, dtype=torch.int32, device=dev)
+    aproj = torch.randn((steps, nb, PROJ), generator=g, device=dev).bfloat16().float()
+    dproj = torch.randn((steps, CP_DN_LAYERS, nb, DN_PROJ), generator=g,
+                        device=dev).bfloat16().float()
+    ones = torch.ones(DIM, device=dev)
+    inv = torch.from_numpy(A.rope_inv_freq()).to(dev)
+    q = torch.empty((nb, Q_HEADS, DIM), device=dev)
+    core = torch.empty_like(q)
+    scratch = A.decode_scratch(nb, device=dev)
+    conv_w, ssm_a, dt, norm_w = dn.w
+    states = [dn.state[layer].unsqueeze(0).repeat(nb, 1, 1, 1).contiguous()
+              for layer in range(CP_DN_LAYERS)]
+    convs = [[dn.conv[layer].unsqueeze(0).repeat(nb, 1, 1).contiguous(),
+              torch.empty((nb, 8192, 3), device=dev)] for layer in range(CP_DN_LAYERS)]
+    dout = torch.empty((nb, 4096), device=dev)
+
+    def step(i):
+        src = aproj[i % steps].data_ptr()
+        pp = capi.AttnPrepBatchedParams(src, src + 8192 * 4, src + 8704 * 4, ones.data_ptr(),
+                                        ones.data_ptr(), inv.data_ptr(), pk_.data_ptr(),
+                                        pv_.data_ptr(), kv_row.data_ptr(), lens.data_ptr(),
+                                        q.data_ptr(), nb, PROJ, EPS)
+        capi.check("prep_batched", lib.miso_attn_prep_batched(ctypes.byref(pp),
+                                                              stream.cuda_stream))
+        dp = capi.AttnDecodeParams(q.data_ptr(), src, pk_.data_ptr(), pv_.data_ptr(),
+                                   kv_row.data_ptr(), lens.data_ptr(), core.data_ptr(), rows, nb,
+                                   PROJ)
+        capi.check("decode", lib.miso_attn_decode(ctypes.byref(dp), scratch.data_ptr(),
+                                                  scratch.numel() * 4, stream.cuda_stream))
+        for layer in range(CP_DN_LAYERS):
+            base = dproj[i % steps, layer].data_ptr()
+            cin, cout = convs[layer][i % 2], convs[layer][1 - i % 2]
+            sp = capi.DeltaNetStepBatchedParams(base, base + 8192 * 4, base + 12288 * 4,
+                                                base + 12320 * 4, conv_w.data_ptr(),
+                                                ssm_a.data_ptr(), dt.data_ptr(), norm_w.data_ptr(),
+                                                cin.data_ptr(), cout.data_ptr(),
+                                                states[layer].data_ptr(), dout.data_ptr(), nb,
+                                                DN_PROJ, EPS)
+            capi.check("dn_step", lib.miso_deltanet_step_batched(ctypes.byref(sp),
+                                                                 stream.cuda_stream))
+
+    for i in range(args.warmup):
+        step(i)
+    lens.fill_(t)
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(steps):
+        step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    barrier()
+    return {"metric": "hybrid block decode tok/s after the prefix", "value":
+            CP_DEC_BATCH * steps / (ms * 1e-3), "unit": "tokens/s", "steps": steps,
+            "ms": ms, "batch": CP_DEC_BATCH, "sequences_per_rank": nb, "context": t,
+            "scaling": "strong", "gpu_launches": steps * (2 + CP_DN_LAYERS)}
 
 
 def bench_cp_block(args, dev, stream, max_over_ranks, barrier, world, rank) -> dict:
@@ -603,19 +701,31 @@ def bench_cp_block(args, dev, stream, max_over_ranks, barrier, world, rank) -> d
     conv_w = (0.5 * torch.randn((8192, 4), generator=g, device=dev)).bfloat16().float()
     ssm_a, dt = -torch.ones(32, device=dev), torch.zeros(32, device=dev)
     norm_w = torch.ones(128, device=dev)
+    # The DeltaNet wavefront runs on its own stream and NCCL communicator, concurrently with the
+    # attention layer (the layers are independent here), so that attention work fills the
+    # wavefront's idle segments.
+    dn_stream = torch.cuda.Stream(device=dev)
+    dn_group = None
+    if world > 1:
+        import torch.distributed as dist
+        dn_group = dist.new_group(list(range(world)), backend="nccl")
     attn = cp.GpuAttentionCp(t, world, rank, proj, ones, ones, inv, EPS, stream)
-    dn = cp.GpuDeltaNetWavefront(t, world, rank, projs, conv_w, ssm_a, dt, norm_w, EPS, stream)
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    dn = cp.GpuDeltaNetWavefront(t, world, rank, projs, conv_w, ssm_a, dt, norm_w, EPS,
+                                 dn_stream, group=dn_group)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
 
     def step(record=False):
         if record:
             ev[0].record(stream)
+        dn_stream.wait_stream(stream)
+        dn.run()
         attn.run()
         if record:
             ev[1].record(stream)
-        dn.run()
+            ev[2].record(dn_stream)
+        stream.wait_stream(dn_stream)
         if record:
-            ev[2].record(stream)
+            ev[3].record(stream)
 
     for _ in range(args.warmup):
         step()
@@ -629,10 +739,12 @@ def bench_cp_block(args, dev, stream, max_over_ranks, barrier, world, rank) -> d
         torch.cuda.synchronize()
         barrier()
         attn_ms += max_over_ranks(ev[0].elapsed_time(ev[1]))
-        dn_ms += max_over_ranks(ev[1].elapsed_time(ev[2]))
-        tot_ms += max_over_ranks(ev[0].elapsed_time(ev[2]))
+        dn_ms += max_over_ranks(ev[0].elapsed_time(ev[2]))
+        tot_ms += max_over_ranks(ev[0].elapsed_time(ev[3]))
     k = args.cp_steps
     attn_ms, dn_ms, tot_ms = attn_ms / k, dn_ms / k, tot_ms / k
+    decode = cp_block_decode(args, dev, stream, max_over_ranks, barrier, world, rank, attn, dn,
+                             dn_group, g)
     a_flops = 8192.0 * t * (t + 1)
     d_flops = CP_DN_LAYERS * 32 * (t // 64) * DN_PREFILL_FLOPS_PER_HEAD_CHUNK
     pk = peaks()
@@ -645,8 +757,13 @@ def bench_cp_block(args, dev, stream, max_over_ranks, barrier, world, rank) -> d
                       "KV all-gather; 3 Gated DeltaNet layers (config 4 shapes) as a state "
                       "hand-off wavefront over contiguous segments",
             "attention": {"ms": attn_ms, "tflops_per_gpu": a_tf / world, "flops": a_flops,
-                          "frac_of_peak_per_gpu": a_tf / world / pk["bf16_tflops"]},
-            "deltanet": {"ms": dn_ms, "flops": d_flops, "layers": CP_DN_LAYERS},
+                          "frac_of_peak_per_gpu": a_tf / world / pk["bf16_tflops"],
+                          "note": "time from the step start to the end of the attention layer, "
+                                  "which shares the GPUs with the concurrent DeltaNet layers"},
+            "deltanet": {"ms": dn_ms, "flops": d_flops, "layers": CP_DN_LAYERS,
+                         "note": "time from the step start to the end of the wavefront (own "
+                                 "stream and NCCL communicator, concurrent with attention)"},
+            "decode": decode,
             "gpu_launches": k * (4 + 3 * CP_DN_LAYERS)}
 
 
@@ -672,6 +789,8 @@ def main():
                     help="tokens of the context-parallel hybrid block (BASELINE config 5)")
     ap.add_argument("--cp-steps", type=int, default=3,
                     help="timed steps of the config 5 block (each is a 131072-token prefill)")
+    ap.add_argument("--cp-decode-steps", type=int, default=CP_DEC_STEPS,
+                    help="decode steps of the config 5 block after the prefix")
     ap.add_argument("--no-cp", action="store_true", help="skip the config 5 block")
     args = ap.parse_args()
     if args.warmup < 3:
