@@ -345,7 +345,12 @@ def run_miso(args) -> None:
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16kv-f32",
         "data": "synthetic", "config": workload_config(world),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"],
-                     "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "traffic": None,
+                     "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
+                     "traffic": (sum(dec_bytes) / len(dec_bytes)) *
+                                DECODE_TRAFFIC_PER_ALGORITHMIC_BYTE,
+                     "traffic_source": "ncu dram read + write of a batch-8 capture "
+                                       "(profiles/decode_kernel_b8_ncu.md) scaled by the KV "
+                                       "bytes of a full launch",
                      "kernel": "decode_kernel", "kernel_ms": dec_avg_ms,
                      "peak_source": pk["source"]},
         "e2e": {"value": world * BATCH / (e2e_ms * 1e-3), "unit": "tokens/s",
@@ -363,6 +368,13 @@ def run_miso(args) -> None:
 
 
 PREFILL_N = 8192
+# ncu DRAM bytes (read + write) per algorithmic byte of the decode kernel: batch-8 capture, 257.0 +
+# 6.3 MB for 256.8 MB of K / V / q / gate (profiles/decode_kernel_b8_ncu.md).
+DECODE_TRAFFIC_PER_ALGORITHMIC_BYTE = (257.0 + 6.3) / 256.8
+# ncu DRAM bytes (read + write) of one full-size launch (profiles/prefill_kernel_8k_ncu.md,
+# profiles/deltanet_prefill_tc_8k_ncu.md).
+PREFILL_8K_TRAFFIC = (221.2 + 102.8) * 1e6
+DN_PREFILL_8K_TRAFFIC = (270.9 + 228.1 + 136.5 + 86.3 + 474.2 + 117.4) * 1e6
 
 
 def prefill_flops(n: int, pos0: int = 0) -> float:
@@ -433,7 +445,8 @@ def bench_prefill(args, dev, stream, max_over_ranks, barrier, world) -> dict:
             "flops_per_step": flops,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"],
                          "unit": "TFLOP/s", "frac": achieved / pk["bf16_tflops"],
-                         "traffic": None, "kernel": "prefill_kernel", "kernel_ms": kern_ms,
+                         "traffic": PREFILL_8K_TRAFFIC if n == 8192 else None,
+                         "kernel": "prefill_kernel", "kernel_ms": kern_ms,
                          "peak_source": pk["source"] + " (dense bf16 burst; fp16 equal)"},
             "gpu_launches": 2 * args.steps}
 
@@ -570,7 +583,8 @@ def bench_deltanet_prefill(args, dev, stream, max_over_ranks, barrier, world) ->
             "flops_per_step": flops, "tflops": tflops, "bytes_per_step": nbytes,
             "gbs": nbytes / (ms * 1e-3) / 1e9,
             "roofline": {"bound": "tensor", "achieved": tflops, "peak": pk["bf16_tflops"],
-                         "unit": "TFLOP/s", "frac": tflops / pk["bf16_tflops"], "traffic": None,
+                         "unit": "TFLOP/s", "frac": tflops / pk["bf16_tflops"],
+                         "traffic": DN_PREFILL_8K_TRAFFIC,
                          "kernel": "conv_kernel + prepare_kernel + recur_kernel", "kernel_ms": ms,
                          "peak_source": pk["source"],
                          "note": "latency-bound: the state recurrence is sequential over the "
