@@ -649,19 +649,19 @@ def cp_block_decode(args, dev, stream, max_over_ranks, barrier, world, rank, att
               torch.empty((nb, 8192, 3), device=dev)] for layer in range(CP_DN_LAYERS)]
     dout = torch.empty((nb, 4096), device=dev)
 
-    def step(i):
+    def step(i, st):
         src = aproj[i % steps].data_ptr()
         pp = capi.AttnPrepBatchedParams(src, src + 8192 * 4, src + 8704 * 4, ones.data_ptr(),
                                         ones.data_ptr(), inv.data_ptr(), pk_.data_ptr(),
                                         pv_.data_ptr(), kv_row.data_ptr(), lens.data_ptr(),
                                         q.data_ptr(), nb, PROJ, EPS)
         capi.check("prep_batched", lib.miso_attn_prep_batched(ctypes.byref(pp),
-                                                              stream.cuda_stream))
+                                                              st.cuda_stream))
         dp = capi.AttnDecodeParams(q.data_ptr(), src, pk_.data_ptr(), pv_.data_ptr(),
                                    kv_row.data_ptr(), lens.data_ptr(), core.data_ptr(), rows, nb,
                                    PROJ)
         capi.check("decode", lib.miso_attn_decode(ctypes.byref(dp), scratch.data_ptr(),
-                                                  scratch.numel() * 4, stream.cuda_stream))
+                                                  scratch.numel() * 4, st.cuda_stream))
         for layer in range(CP_DN_LAYERS):
             base = dproj[i % steps, layer].data_ptr()
             cin, cout = convs[layer][i % 2], convs[layer][1 - i % 2]
@@ -672,22 +672,32 @@ def cp_block_decode(args, dev, stream, max_over_ranks, barrier, world, rank, att
                                                 states[layer].data_ptr(), dout.data_ptr(), nb,
                                                 DN_PROJ, EPS)
             capi.check("dn_step", lib.miso_deltanet_step_batched(ctypes.byref(sp),
-                                                                 stream.cuda_stream))
+                                                                 st.cuda_stream))
 
     for i in range(args.warmup):
-        step(i)
+        step(i, stream)
+    torch.cuda.synchronize()
+    # The 256 steps (5 launches each, one token per sequence) are captured once into a CUDA graph
+    # and replayed, so the host's per-launch cost does not pace one-sequence-per-rank decoding.
+    graph = torch.cuda.CUDAGraph()
+    cap_stream = torch.cuda.Stream(device=dev)
+    cap_stream.wait_stream(stream)
+    with torch.cuda.graph(graph, stream=cap_stream):
+        for i in range(steps):
+            step(i, cap_stream)
     lens.fill_(t)
     torch.cuda.synchronize()
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for i in range(steps):
-        step(i)
-    e1.record(stream)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        graph.replay()
+        e1.record(stream)
     torch.cuda.synchronize()
     barrier()
     ms = max_over_ranks(e0.elapsed_time(e1))
     barrier()
+    del graph
     return {"metric": "hybrid block decode tok/s after the prefix", "value":
             CP_DEC_BATCH * steps / (ms * 1e-3), "unit": "tokens/s", "steps": steps,
             "ms": ms, "batch": CP_DEC_BATCH, "sequences_per_rank": nb, "context": t,
@@ -718,7 +728,9 @@ def bench_cp_block(args, dev, stream, max_over_ranks, barrier, world, rank) -> d
     # The DeltaNet wavefront runs on its own stream and NCCL communicator, concurrently with the
     # attention layer (the layers are independent here), so that attention work fills the
     # wavefront's idle segments.
-    dn_stream = torch.cuda.Stream(device=dev)
+    # Higher priority: when attention CTAs retire, the block scheduler starts the wavefront's
+    # CTAs first, so the sequential DeltaNet chain is not queued behind the whole attention grid.
+    dn_stream = torch.cuda.Stream(device=dev, priority=-1)
     dn_group = None
     if world > 1:
         import torch.distributed as dist
