@@ -88,6 +88,18 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int sit
   }
 }
 
+// Non-blocking test of the phase with the given parity.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Orders this thread's generic-proxy shared-memory writes before later async-proxy (TMA) writes.
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

@@ -16,7 +16,7 @@
 //                      the max grows by more than 2^8, then exactly), P = 2^(s - m) as fp16
 //                      into 128B-swizzled shared memory
 //   O += P_j V_j       tcgen05.mma M=128 N=256 K=64 (4 x K16), A = P (K-major), B = V (MN-major)
-// Roles: warp 0 issues TMA (Q once; K, V double-buffered), warp 1 owns TMEM and issues every MMA
+// Roles: warps 0 and 2 issue TMA (Q and K; V; both double-buffered), warp 1 owns TMEM and issues every MMA
 // from one thread, warps 4-11 run softmax, O correction and the epilogue (O / l * sigmoid(gate),
 // each warp staging its 32 rows through shared memory so global stores and gate loads are
 // row-contiguous). Control decisions inside a softmax warp are warp-uniform (__all_sync), as the
@@ -44,7 +44,7 @@ constexpr int kQHeads = 16, kKvHeads = 2, kDim = 256, kGroup = 8;
 constexpr int kTokens = 16;  // tokens per query tile; x 8 heads = 128 rows
 constexpr int kRows = 128;
 constexpr int kBN = 64;  // keys per KV tile
-constexpr int kThreads = 384;  // warp 0 TMA, warp 1 MMA + TMEM, warps 4-11 softmax
+constexpr int kThreads = 384;  // warps 0 / 2 TMA, warp 1 MMA + TMEM, warps 4-11 softmax
 constexpr uint32_t kQBox = kRows * 64 * 2;      // one 64-dim slab of Q: 16 KB
 constexpr uint32_t kKVBox = kBN * 64 * 2;       // one 64-dim slab of a K / V tile: 8 KB
 constexpr uint32_t kQBytes = 4 * kQBox;         // 64 KB
@@ -126,7 +126,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       dev::mbar_init(dev::smem_u32(&bar.p_full[s]), 8);
       dev::mbar_init(dev::smem_u32(&bar.pv_done[s]), 1);
       for (int qd = 0; qd < 4; ++qd)
-        dev::mbar_init(dev::smem_u32(&bar.xchg[qd][s]), 64);
+        dev::mbar_init(dev::smem_u32(&bar.xchg[qd][s]), 2);
     }
     dev::mbar_init(dev::smem_u32(&bar.drain), 1);
     bar.abort_flag = 0;
@@ -141,42 +141,42 @@ __global__ void __launch_bounds__(kThreads, 1)
   dev::tc_fence_after();
   const uint32_t tmem = bar.tmem_base;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------------------------ producer
+  if (warp == 0 || warp == 2) {
+    // ------------------------------------------------------------------------------ producers
+    // Warp 0 loads Q and the K tiles, warp 2 the V tiles: the two streams refill independently
+    // (K_j as soon as S_(j-2) has released its stage, V_j as soon as PV_(j-2) has) and each
+    // producer blocks in a suspending wait.
     if (lane == 0) {
-      dev::tma_prefetch_desc(&qmap);
-      dev::tma_prefetch_desc(&kmap);
-      dev::tma_prefetch_desc(&vmap);
-      dev::mbar_arrive_expect_tx(dev::smem_u32(&bar.q_full), kQBytes);
-      for (int box = 0; box < 4; ++box)
-        dev::tma_load_3d(sbase + kOffQ + box * kQBox, &qmap, box * 64, kvh * kGroup, t0,
-                         dev::smem_u32(&bar.q_full));
+      const bool is_k = warp == 0;
+      const CUtensorMap* map = is_k ? &kmap : &vmap;
+      uint64_t* full = is_k ? bar.k_full : bar.v_full;
+      uint64_t* empty = is_k ? bar.k_empty : bar.v_empty;
+      const uint32_t dst0 = sbase + (is_k ? kOffK : kOffV);
+      dev::tma_prefetch_desc(map);
+      if (is_k) {
+        dev::tma_prefetch_desc(&qmap);
+        dev::mbar_arrive_expect_tx(dev::smem_u32(&bar.q_full), kQBytes);
+        for (int box = 0; box < 4; ++box)
+          dev::tma_load_3d(sbase + kOffQ + box * kQBox, &qmap, box * 64, kvh * kGroup, t0,
+                           dev::smem_u32(&bar.q_full));
+      }
       unsigned issued = 0;
       for (unsigned j = 0; j < nkv; ++j) {
         const unsigned s = j & 1, ph = (j >> 1) & 1;
-        if (j >= 2 && !wait_or_abort(bar, bar.k_empty[s], ph ^ 1))
+        if (j >= 2 && !wait_or_abort(bar, empty[s], ph ^ 1))
           break;
-        dev::mbar_arrive_expect_tx(dev::smem_u32(&bar.k_full[s]), kKVBytes);
+        dev::mbar_arrive_expect_tx(dev::smem_u32(&full[s]), kKVBytes);
         for (int box = 0; box < 4; ++box)
-          dev::tma_load_3d(sbase + kOffK + s * kKVBytes + box * kKVBox, &kmap, box * 64, j * kBN,
-                           kvh, dev::smem_u32(&bar.k_full[s]));
-        if (j >= 2 && !wait_or_abort(bar, bar.v_empty[s], ph ^ 1)) {
-          issued = 2 * j + 1;
-          break;
-        }
-        dev::mbar_arrive_expect_tx(dev::smem_u32(&bar.v_full[s]), kKVBytes);
-        for (int box = 0; box < 4; ++box)
-          dev::tma_load_3d(sbase + kOffV + s * kKVBytes + box * kKVBox, &vmap, box * 64, j * kBN,
-                           kvh, dev::smem_u32(&bar.v_full[s]));
-        issued = 2 * j + 2;
+          dev::tma_load_3d(dst0 + s * kKVBytes + box * kKVBox, map, box * 64, j * kBN, kvh,
+                           dev::smem_u32(&full[s]));
+        issued = j + 1;
       }
       if (aborted(bar)) {
         // Let the copies already issued land before the CTA exits (bounded waits).
-        dev::mbar_wait(dev::smem_u32(&bar.q_full), 0);
-        for (unsigned c = issued >= 4 ? issued - 4 : 0; c < issued; ++c) {
-          const unsigned j = c / 2, s = j & 1, ph = (j >> 1) & 1;
-          dev::mbar_wait(dev::smem_u32(c % 2 == 0 ? &bar.k_full[s] : &bar.v_full[s]), ph);
-        }
+        if (is_k)
+          dev::mbar_wait(dev::smem_u32(&bar.q_full), 0);
+        for (unsigned j = issued >= 2 ? issued - 2 : 0; j < issued; ++j)
+          dev::mbar_wait(dev::smem_u32(&full[j & 1]), (j >> 1) & 1);
       }
     }
   } else if (warp == 1) {
@@ -191,38 +191,57 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t vdesc0 = dev::sdesc_sw128(sbase + kOffV, kKVBox, 1024);
       bool ok = wait_or_abort(bar, bar.q_full, 0);
       dev::tc_fence_after();
-      for (unsigned j = 0; ok && j <= nkv; ++j) {
-        if (j < nkv) {
-          const unsigned s = j & 1, ph = (j >> 1) & 1;
-          if (!wait_or_abort(bar, bar.k_full[s], ph) ||
-              (j >= 2 && !wait_or_abort(bar, bar.s_free[s], ph ^ 1))) {
-            ok = false;
-            break;
-          }
-          dev::tc_fence_after();
-          const uint32_t d = tmem + kColS + s * kBN;
-          const uint64_t kd = kdesc0 + ((s * kKVBytes) >> 4);
+      // Issue state machine: S(j) goes out as soon as K_j has landed and S buffer j & 1 has been
+      // read by softmax(j - 2); PV(i) as soon as P_i and V_i are ready. Both are polled, so a PV
+      // is never held back behind the next K tile's load (the S / PV order in the tensor pipe
+      // does not matter: they write different TMEM columns; the PVs stay in order).
+      unsigned ns = 0, np = 0;  // next S and next PV to issue
+      long long last = clock64();
+      while (ok && np < nkv) {
+        bool progressed = false;
+        if (ns < nkv) {
+          const unsigned s = ns & 1, ph = (ns >> 1) & 1;
+          if (dev::mbar_test_wait(dev::smem_u32(&bar.k_full[s]), ph) &&
+              (ns < 2 || dev::mbar_test_wait(dev::smem_u32(&bar.s_free[s]), ph ^ 1))) {
+            dev::tc_fence_after();
+            const uint32_t d = tmem + kColS + s * kBN;
+            const uint64_t kd = kdesc0 + ((s * kKVBytes) >> 4);
 #pragma unroll
-          for (int ks = 0; ks < kDim / 16; ++ks)
-            dev::tc_mma_f16_ss(d, qdesc0 + (((ks >> 2) * kQBox + (ks & 3) * 32) >> 4),
-                               kd + (((ks >> 2) * kKVBox + (ks & 3) * 32) >> 4), idesc_s, ks > 0);
-          dev::tc_commit(dev::smem_u32(&bar.s_full[s]));
-          dev::tc_commit(dev::smem_u32(&bar.k_empty[s]));
+            for (int ks = 0; ks < kDim / 16; ++ks)
+              dev::tc_mma_f16_ss(d, qdesc0 + (((ks >> 2) * kQBox + (ks & 3) * 32) >> 4),
+                                 kd + (((ks >> 2) * kKVBox + (ks & 3) * 32) >> 4), idesc_s, ks > 0);
+            dev::tc_commit(dev::smem_u32(&bar.s_full[s]));
+            dev::tc_commit(dev::smem_u32(&bar.k_empty[s]));
+            ++ns;
+            progressed = true;
+          }
         }
-        if (j >= 1) {
-          const unsigned i = j - 1, s = i & 1, ph = (i >> 1) & 1;
-          if (!wait_or_abort(bar, bar.p_full[s], ph) || !wait_or_abort(bar, bar.v_full[s], ph)) {
-            ok = false;
-            break;
-          }
-          dev::tc_fence_after();
-          const uint64_t pd = pdesc0 + ((s * kPBytes) >> 4), vd = vdesc0 + ((s * kKVBytes) >> 4);
+        if (np < ns) {
+          const unsigned i = np, s = i & 1, ph = (i >> 1) & 1;
+          if (dev::mbar_test_wait(dev::smem_u32(&bar.p_full[s]), ph) &&
+              dev::mbar_test_wait(dev::smem_u32(&bar.v_full[s]), ph)) {
+            dev::tc_fence_after();
+            const uint64_t pd = pdesc0 + ((s * kPBytes) >> 4), vd = vdesc0 + ((s * kKVBytes) >> 4);
 #pragma unroll
-          for (int kk = 0; kk < kBN / 16; ++kk)
-            dev::tc_mma_f16_ss(tmem + kColO, pd + ((kk * 32) >> 4), vd + ((kk * 2048) >> 4),
-                               idesc_o, (i > 0 || kk > 0) ? 1u : 0u);
-          dev::tc_commit(dev::smem_u32(&bar.pv_done[s]));
-          dev::tc_commit(dev::smem_u32(&bar.v_empty[s]));
+            for (int kk = 0; kk < kBN / 16; ++kk)
+              dev::tc_mma_f16_ss(tmem + kColO, pd + ((kk * 32) >> 4), vd + ((kk * 2048) >> 4),
+                                 idesc_o, (i > 0 || kk > 0) ? 1u : 0u);
+            dev::tc_commit(dev::smem_u32(&bar.pv_done[s]));
+            dev::tc_commit(dev::smem_u32(&bar.v_empty[s]));
+            ++np;
+            progressed = true;
+          }
+        }
+        if (progressed) {
+          last = clock64();
+        } else if (aborted(bar)) {
+          ok = false;
+        } else if (clock64() - last > dev::kWaitLimitCycles) {  // nothing became ready: give up
+          dev::set_status(dev::kStatusTimeout, 0x21);
+          bar.abort_flag = 1;
+          ok = false;
+        } else {
+          __nanosleep(20);  // short: this thread is on the critical path, but shares issue slots
         }
       }
       // Every MMA issued above has completed once `drain` flips (bounded).
@@ -244,11 +263,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float kNegInf = -__int_as_float(0x7f800000);
     float m_ref = kNegInf, l = 0.0f;
     bool ok = true;
-    // Exchange of one float per row with the partner warp through red[] and an mbarrier of
-    // 64 arrivals (bounded wait); returns the partner's value.
+    // Exchange of one float per row with the partner warp through red[] and an mbarrier with
+    // one arrival per warp (bounded wait); returns the partner's value.
     auto exchange = [&](unsigned j, float mine, float& theirs) -> bool {
       red[((j & 1) * 2 + hc) * kRows + r] = mine;
-      dev::mbar_arrive(dev::smem_u32(&bar.xchg[q][j & 1]));
+      __syncwarp();
+      if (lane == 0)
+        dev::mbar_arrive(dev::smem_u32(&bar.xchg[q][j & 1]));
       if (!__all_sync(0xffffffffu, wait_or_abort(bar, bar.xchg[q][j & 1], (j >> 1) & 1)))
         return false;
       theirs = red[((j & 1) * 2 + (1 - hc)) * kRows + r];
@@ -268,19 +289,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0)
         dev::mbar_arrive(dev::smem_u32(&bar.s_free[s]));
+      // Raw scores (the scale is folded into the exponent's FMA below; it is positive, so the
+      // maximum commutes with it).
       const unsigned key0 = j * kBN + 32 * hc;
       float v[32];
       float mx = kNegInf;
       if (key0 + 31 <= pos_min) {  // interior tile half: no masking
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
-          v[c] = __uint_as_float(x[c]) * sl2;
+          v[c] = __uint_as_float(x[c]);
           mx = fmaxf(mx, v[c]);
         }
       } else {
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
-          v[c] = key0 + c <= pos ? __uint_as_float(x[c]) * sl2 : kNegInf;
+          v[c] = key0 + c <= pos ? __uint_as_float(x[c]) : kNegInf;
           mx = fmaxf(mx, v[c]);
         }
       }
@@ -289,7 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = false;
         break;
       }
-      const float m_new = fmaxf(m_ref, fmaxf(mx, mx_other));
+      const float m_new = fmaxf(m_ref, fmaxf(mx, mx_other) * sl2);
       if (j == 0) {
         m_ref = m_new;  // O is written (not accumulated) by the first P V
       } else if (__any_sync(0xffffffffu, m_new > m_ref + 8.0f)) {
@@ -322,21 +345,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       uint8_t* prow = base + kOffP + s * kPBytes + r * 128;
-      float lsum = 0.0f;
+      const float neg_m = -m_ref;
+      float lsum0 = 0.0f, lsum1 = 0.0f;
 #pragma unroll
       for (int c4 = 0; c4 < 4; ++c4) {
         __align__(16) __half2 h[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float p0 = dev::ex2_approx(v[8 * c4 + 2 * e] - m_ref);
-          const float p1 = dev::ex2_approx(v[8 * c4 + 2 * e + 1] - m_ref);
+          const float p0 = dev::ex2_approx(fmaf(v[8 * c4 + 2 * e], sl2, neg_m));
+          const float p1 = dev::ex2_approx(fmaf(v[8 * c4 + 2 * e + 1], sl2, neg_m));
           h[e] = __floats2half2_rn(p0, p1);
-          lsum += p0 + p1;
+          lsum0 += p0;
+          lsum1 += p1;
         }
         *reinterpret_cast<uint4*>(prow + (((4 * hc + c4) ^ (r & 7)) << 4)) =
             *reinterpret_cast<const uint4*>(h);
       }
-      l += lsum;
+      l += lsum0 + lsum1;
       dev::fence_proxy_async_smem();
       dev::tc_fence_before();
       __syncwarp();
