@@ -503,11 +503,11 @@ int miso_deltanet_step_batched(const miso_deltanet_step_batched_params* p, void*
 }
 
 // Scratch of miso_deltanet_prefill_tc, each part 1024-byte aligned: q16, k16 [n][16][128] and
-// v16 [n][32][128] fp16 with their fp16 remainders, beta, log_a, e^g, e^(g_last - g) [32][np]
-// fp32, Tw, Tu, Aqk and its remainder [32][nc][64][64] fp16
+// v16 [n][32][128] fp16 with their fp16 remainders, beta, log_a, e^g [32][np] fp32, W, Ks, Qg
+// [32][nc][64][128] fp16, Tu, Aqk and its remainder [32][nc][64][64] fp16
 // (np = 64 nc, nc = ceil(n / 64)).
 struct DnChunkScratch {
-  size_t q16, k16, v16, q16lo, k16lo, v16lo, beta, loga, eg, egl, tw, tu, aqk, aqklo, total;
+  size_t q16, k16, v16, q16lo, k16lo, v16lo, beta, loga, eg, w, ks, qg, tu, aqk, aqklo, total;
 };
 
 static DnChunkScratch dn_chunk_scratch(unsigned n) {
@@ -524,8 +524,9 @@ static DnChunkScratch dn_chunk_scratch(unsigned n) {
   s.beta = o, o += up(32 * np * 4);
   s.loga = o, o += up(32 * np * 4);
   s.eg = o, o += up(32 * np * 4);
-  s.egl = o, o += up(32 * np * 4);
-  s.tw = o, o += up(32 * nc * 64 * 64 * 2);
+  s.w = o, o += up(32 * nc * 64 * 128 * 2);
+  s.ks = o, o += up(32 * nc * 64 * 128 * 2);
+  s.qg = o, o += up(32 * nc * 64 * 128 * 2);
   s.tu = o, o += up(32 * nc * 64 * 64 * 2);
   s.aqk = o, o += up(32 * nc * 64 * 64 * 2);
   s.aqklo = o, o += up(32 * nc * 64 * 64 * 2);
@@ -568,14 +569,15 @@ int miso_deltanet_prefill_tc(const miso_deltanet_seq_params* p, void* scratch, s
   float* beta = reinterpret_cast<float*>(base + L.beta);
   float* loga = reinterpret_cast<float*>(base + L.loga);
   float* eg = reinterpret_cast<float*>(base + L.eg);
-  float* egl = reinterpret_cast<float*>(base + L.egl);
-  __half* tw = reinterpret_cast<__half*>(base + L.tw);
+  __half* w = reinterpret_cast<__half*>(base + L.w);
+  __half* ks = reinterpret_cast<__half*>(base + L.ks);
+  __half* qg = reinterpret_cast<__half*>(base + L.qg);
   __half* tu = reinterpret_cast<__half*>(base + L.tu);
   __half* aqk = reinterpret_cast<__half*>(base + L.aqk);
   __half* aqklo = reinterpret_cast<__half*>(base + L.aqklo);
   const unsigned nc = (p->n + 63) / 64, np = 64 * nc;
 
-  CUtensorMap qmap, kmap, qlmap, klmap, vmap, vlmap, twmap, tumap, aqkmap, aqklmap;
+  CUtensorMap qmap, kmap, qlmap, klmap, vmap, vlmap, tumap, aqkmap, aqklmap, wmap, ksmap, qgmap;
   {
     const cuuint64_t dims[3] = {128, 16, p->n};
     const cuuint64_t strides[2] = {128 * 2, 16 * 128 * 2};
@@ -598,10 +600,18 @@ int miso_deltanet_prefill_tc(const miso_deltanet_seq_params* p, void* scratch, s
     const cuuint64_t dims[2] = {64, uint64_t(32) * nc * 64};
     const cuuint64_t strides[1] = {64 * 2};
     const cuuint32_t box[2] = {64, 64};
-    if ((st = f16_map(&twmap, tw, 2, dims, strides, box)) != MISO_OK ||
-        (st = f16_map(&tumap, tu, 2, dims, strides, box)) != MISO_OK ||
+    if ((st = f16_map(&tumap, tu, 2, dims, strides, box)) != MISO_OK ||
         (st = f16_map(&aqkmap, aqk, 2, dims, strides, box)) != MISO_OK ||
         (st = f16_map(&aqklmap, aqklo, 2, dims, strides, box)) != MISO_OK)
+      return st;
+  }
+  {
+    const cuuint64_t dims[2] = {128, uint64_t(32) * nc * 64};
+    const cuuint64_t strides[1] = {128 * 2};
+    const cuuint32_t box[2] = {64, 64};
+    if ((st = f16_map(&wmap, w, 2, dims, strides, box)) != MISO_OK ||
+        (st = f16_map(&ksmap, ks, 2, dims, strides, box)) != MISO_OK ||
+        (st = f16_map(&qgmap, qg, 2, dims, strides, box)) != MISO_OK)
       return st;
   }
   cudaStream_t s = as_stream(stream);
@@ -636,8 +646,9 @@ int miso_deltanet_prefill_tc(const miso_deltanet_seq_params* p, void* scratch, s
   pa.beta = beta;
   pa.loga = loga;
   pa.eg = eg;
-  pa.egl = egl;
-  pa.tw = tw;
+  pa.w = w;
+  pa.ks = ks;
+  pa.qg = qg;
   pa.tu = tu;
   pa.aqk = aqk;
   pa.aqklo = aqklo;
@@ -651,7 +662,6 @@ int miso_deltanet_prefill_tc(const miso_deltanet_seq_params* p, void* scratch, s
 
   dc::RecurArgs ra;
   ra.eg = eg;
-  ra.egl = egl;
   ra.z = p->z;
   ra.norm_w = p->norm_w;
   ra.state = p->state;
@@ -660,10 +670,9 @@ int miso_deltanet_prefill_tc(const miso_deltanet_seq_params* p, void* scratch, s
   ra.np = np;
   ra.nc = nc;
   ra.zab_stride = p->zab_stride;
-  ra.z_prefetch = aligned16(p->z) && p->zab_stride % 4 == 0;
   ra.eps = p->eps;
   dc::recur_kernel<<<32, dc::kRecurThreads, dc::kRecurSmemBytes, s>>>(
-      qmap, kmap, vmap, vlmap, twmap, tumap, aqkmap, aqklmap, ra);
+      wmap, qgmap, ksmap, vmap, vlmap, tumap, aqkmap, aqklmap, ra);
   return launch_status();
 }
 

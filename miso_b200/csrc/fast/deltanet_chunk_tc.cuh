@@ -17,23 +17,26 @@
 // Three launches:
 //   conv_kernel     one block per (1024 channels, 16 tokens): 4-tap causal conv + SiLU, q / k
 //                   L2 norms (q also * 1/sqrt(128)), beta, log alpha; writes q, k, v as fp16
-//                   and the final conv history.
-//   prepare_kernel  one block per (chunk, K head), both V heads of the K head: [K; Q] K^T as one
-//                   tcgen05 MMA (M=128, N=64, K=128), L and Aqk from it, T = (I + L)^-1 by
-//                   forward substitution (thread per column), Tw = T diag(beta e^g),
-//                   Tu = T diag(beta) and Aqk as fp16 tiles, e^g and e^(g_last - g) as fp32.
-//   recur_kernel    one block per V head, the 128 x 128 state transposed (S^T: lane = v, column =
-//                   k) as an fp32 TMEM accumulator; per chunk five tcgen05 MMA groups with M = 128:
-//                     W^T = K^T Tw^T, U^T = V^T Tu^T    (from this chunk's inputs only)
-//                     X^T = S^T W^T,  Y^T = S^T Q^T     (A = S^T as fp16 in shared memory)
-//                     S^T += (delta^T diag(e^(g_last - g))) K
-//                     Z^T = delta^T Aqk^T
-//                   and the epilogues delta^T = U^T - X^T, O^T = diag(e^g) Y^T + Z^T (+ norm,
-//                   gate, store) on CUDA cores.
+//                   high parts and fp16 remainders, and the final conv history.
+//   prepare_kernel  one block per (chunk, K head), both V heads of the K head: everything of the
+//                   chunk that does not depend on the state. [K; Q] K^T as one tcgen05 MMA
+//                   (M=128, N=64, K=128) over hi / lo operands, L and Aqk from it, T = (I + L)^-1
+//                   by blocked forward substitution, then W = [Tw_0; Tw_1] K for both V heads as
+//                   one M=128 MMA; writes W, Ks = K rows * e^(g_last - g), Qg = Q rows * e^g,
+//                   Tu = T diag(beta), Aqk (hi + lo) as fp16 tiles and e^g.
+//   recur_kernel    one block per V head (640 threads), the 128 x 128 state transposed (S^T:
+//                   lane = v, column = k) as an fp32 TMEM accumulator; per chunk, tcgen05 MMA
+//                   groups with M = 128 whose A operands (S^T, delta^T as fp16) live in TMEM:
+//                     [X^T | O^T] = S^T [W; Qg]^T                  (one N = 128 product)
+//                     U^T = (V_hi + V_lo)^T Tu^T                   (one chunk ahead)
+//                     S^T += delta^T Ks,  O^T += delta^T Aqk^T     (delta, Aqk as hi + lo)
+//                   and the CUDA-core epilogues delta^T = U^T - X^T and the gated RMS norm of O.
 //
-// Precision: every MMA accumulates in fp32 and the state stays fp32 in TMEM; the operands (q, k,
-// v, T, Aqk, the fp16 copy of S^T read by X / Y, delta) are fp16, whose 11-bit significand keeps
-// the outputs within ~1e-4 relative of an fp64 recurrence.
+// Precision: every MMA accumulates in fp32 and the state stays fp32 in TMEM. The products whose
+// rounding reaches the outputs through cancelling sums (q . k, Aqk delta, U) use two-term fp16
+// operands (hi + lo), the others plain fp16 (W, Ks, Qg and the S^T copy are rounded once from
+// fp32); outputs stay within ~1e-4 relative (~6e-3 absolute at 8192 tokens) of an fp64
+// recurrence.
 //
 // Every mbarrier wait is bounded; on a timeout the block records MISO_STATUS_TIMEOUT (site 0x30 /
 // 0x31), stops issuing, drains what it issued and frees its TMEM before exiting.
@@ -196,24 +199,27 @@ struct PrepareArgs {
   const float* beta;  // [32][np]
   const float* loga;  // [32][np]
   float* eg;          // [32][np] e^(g_t), g = in-chunk cumulative log decay (0 past n)
-  float* egl;         // [32][np] e^(g_last - g_t), g_last that of the chunk's row 63
-  __half* tw;         // [32][nc][64][64]
-  __half* tu;
-  __half* aqk;        // Aqk as fp16 high part ...
+  __half* w;          // [32][nc][64][128] W = T diag(beta e^g) K
+  __half* ks;         // [32][nc][64][128] K rows * e^(g_last - g_j)
+  __half* qg;         // [32][nc][64][128] Q rows * e^(g_i)
+  __half* tu;         // [32][nc][64][64] T diag(beta)
+  __half* aqk;        // [32][nc][64][64] Aqk as fp16 high part ...
   __half* aqklo;      // ... and fp16 remainder
   unsigned n, np, nc;
 };
 
 constexpr int kPrepThreads = 128;
 constexpr int kLRow = 68;  // fp32 row stride of L (16-byte aligned rows)
-constexpr int kTRow = 65;  // fp32 stride of a solved column of T (conflict-free per lane)
-static_assert((2 * 64 * kTRow + 4 * 64) * 4 <= 8 * 8192, "T columns fit in the [K; Q] tile area");
 // [K; Q] as fp16 high parts (32 KB) then remainders (32 KB): 64-dim slab s of part p at
 // 32 KB p + 16 KB s, K rows first, Q rows 8 KB later (M = 128 rows).
 constexpr uint32_t kPrepOffL = 8 * kTile;
-constexpr uint32_t kPrepOffG = kPrepOffL + 2 * kC * kLRow * 4;     // g[2][64], beta[2][64]
-constexpr uint32_t kPrepOffBar = kPrepOffG + 4 * kC * 4;
+constexpr uint32_t kPrepOffG = kPrepOffL + 2 * kC * kLRow * 4;  // g, beta, fac, e^g, e^(gl-g)
+constexpr uint32_t kPrepOffBar = kPrepOffG + 12 * kC * 4;
 constexpr size_t kPrepSmemBytes = kPrepOffBar + 64;
+// Solved T (fp32 [2 heads][64 rows i][64 columns j]) reuses the remainder half of the tile area,
+// and [Tw_0; Tw_1] (fp16 [128 rows][64], 128-byte swizzled, the A operand of W) the L area.
+static_assert(2 * kC * kC * 4 <= 4 * kTile, "T fits in the remainder tiles");
+static_assert(2 * kTile <= 2 * kC * kLRow * 4, "[Tw_0; Tw_1] fits in the L area");
 
 __global__ void __launch_bounds__(kPrepThreads, 2)
     prepare_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
@@ -230,19 +236,22 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
   const uint32_t sbase = dev::smem_u32(smem);
   float* Ls = reinterpret_cast<float*>(smem + kPrepOffL);  // [2][64][kLRow]
   float* gs = reinterpret_cast<float*>(smem + kPrepOffG);  // [2][64]
-  float* bs = gs + 2 * kC;                                 // [2][64]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kPrepOffBar);  // load, mma
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2);
-  int* fail = reinterpret_cast<int*>(bars + 3);
+  float* bs = gs + 2 * kC;                                 // [2][64] beta
+  float* fac = bs + 2 * kC;                                // [2][2][64] beta e^g, beta
+  float* egs = fac + 4 * kC;                               // [2][64] e^g
+  float* egls = egs + 2 * kC;                              // [2][64] e^(g_last - g)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kPrepOffBar);  // load, KK^T, W
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3);
+  int* fail = reinterpret_cast<int*>(bars + 4);
 
   if (tid == 0) {
-    dev::mbar_init(dev::smem_u32(&bars[0]), 1);
-    dev::mbar_init(dev::smem_u32(&bars[1]), 1);
+    for (int i = 0; i < 3; ++i)
+      dev::mbar_init(dev::smem_u32(&bars[i]), 1);
     *fail = 0;
     dev::mbar_init_fence();
   }
   if (warp == 0) {
-    dev::tmem_alloc(dev::smem_u32(tmem_slot), 64);
+    dev::tmem_alloc(dev::smem_u32(tmem_slot), 128);
     dev::tmem_relinquish();
   }
   dev::tc_fence_before();
@@ -275,14 +284,17 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
     }
     const float g0 = incl - l1, g1 = incl;
     const float glast = __shfl_sync(0xffffffffu, incl, 31);
-    gs[warp * kC + 2 * lane] = g0;
-    gs[warp * kC + 2 * lane + 1] = g1;
-    bs[warp * kC + 2 * lane] = t0 < a.n ? a.beta[size_t(h) * a.np + t0] : 0.0f;
-    bs[warp * kC + 2 * lane + 1] = t0 + 1 < a.n ? a.beta[size_t(h) * a.np + t0 + 1] : 0.0f;
-    *reinterpret_cast<float2*>(a.eg + size_t(h) * a.np + t0) =
-        make_float2(__expf(g0), __expf(g1));
-    *reinterpret_cast<float2*>(a.egl + size_t(h) * a.np + t0) =
-        make_float2(__expf(glast - g0), __expf(glast - g1));
+    const unsigned i0 = warp * kC + 2 * lane;
+    gs[i0] = g0;
+    gs[i0 + 1] = g1;
+    bs[i0] = t0 < a.n ? a.beta[size_t(h) * a.np + t0] : 0.0f;
+    bs[i0 + 1] = t0 + 1 < a.n ? a.beta[size_t(h) * a.np + t0 + 1] : 0.0f;
+    const float e0 = __expf(g0), e1 = __expf(g1);
+    egs[i0] = e0;
+    egs[i0 + 1] = e1;
+    egls[i0] = __expf(glast - g0);
+    egls[i0 + 1] = __expf(glast - g1);
+    *reinterpret_cast<float2*>(a.eg + size_t(h) * a.np + t0) = make_float2(e0, e1);
   }
   if (tid == 0) {
     if (dev::mbar_wait(dev::smem_u32(&bars[0]), 0, 0x31)) {
@@ -361,16 +373,15 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
   // T = (I + L)^-1 by forward substitution, thread (hh, col) solving column col of V head
   // kh + 16 hh: t_i = [i == col] - sum_{j<i} L_ij t_j. Rows go in blocks of 16: first the
   // contributions of all earlier rows to the block's 16 rows (16 independent accumulators), then
-  // the block's own 16 x 16 triangle. Solved columns live in shared memory (Tc, in the [K; Q]
-  // tile area, free once the MMA has completed), which keeps the code compact.
-  float* Tc = reinterpret_cast<float*>(smem);  // [2][64 cols][kTRow]
-  float* fac = Tc + 2 * kC * kTRow;            // [2][2][64]: beta e^g (Tw), beta (Tu) per column
+  // the block's own 16 x 16 triangle. T is kept as [hh][i][col] (a lane's column is its bank) in
+  // the remainder tiles, free once the MMA has completed; the K and Q high parts stay in place.
+  float* Tc = reinterpret_cast<float*>(smem + 4 * kTile);  // [2][64 rows][64 cols]
   if (ok) {
     const unsigned hh = tid / kC, col = tid % kC;
     const float* L = Ls + hh * kC * kLRow;
-    float* tcol = Tc + (hh * kC + col) * kTRow;
+    float* tcol = Tc + hh * kC * kC + col;  // row i at tcol[i * kC]
     const float bc = bs[hh * kC + col];
-    fac[(hh * 2 + 0) * kC + col] = bc * __expf(gs[hh * kC + col]);
+    fac[(hh * 2 + 0) * kC + col] = bc * egs[hh * kC + col];
     fac[(hh * 2 + 1) * kC + col] = bc;
 #pragma unroll 1
     for (int b = 0; b < kC / 16; ++b) {
@@ -381,7 +392,8 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
         acc[r] = i0 + r == int(col) ? 1.0f : 0.0f;
 #pragma unroll 1
       for (int j = 0; j < i0; j += 4) {
-        const float t0 = tcol[j], t1 = tcol[j + 1], t2 = tcol[j + 2], t3 = tcol[j + 3];
+        const float t0 = tcol[j * kC], t1 = tcol[(j + 1) * kC], t2 = tcol[(j + 2) * kC],
+                    t3 = tcol[(j + 3) * kC];
 #pragma unroll
         for (int r = 0; r < 16; ++r) {
           const float4 l4 = *reinterpret_cast<const float4*>(L + (i0 + r) * kLRow + j);
@@ -395,32 +407,100 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
           acc[r] -= L[(i0 + r) * kLRow + i0 + q] * acc[q];
 #pragma unroll
       for (int r = 0; r < 16; ++r)
-        tcol[i0 + r] = acc[r];
+        tcol[(i0 + r) * kC] = acc[r];
     }
   }
   __syncthreads();
+  uint8_t* twt = smem + kPrepOffL;  // [Tw_0; Tw_1]: [128 rows (hh, i)][64 j] fp16, swizzled
   if (ok) {
-    // Tw = T diag(beta e^g), Tu = T diag(beta) as fp16 rows: 16-byte chunk (hh, which, i, k)
-    // holds columns 8k .. 8k + 7 of row i.
-    for (unsigned u = tid; u < 2 * 2 * kC * 8; u += kPrepThreads) {
-      const unsigned k = u % 8, i = (u / 8) % kC, which = (u / (8 * kC)) % 2, hh = u / (16 * kC);
-      const float* f = fac + (hh * 2 + which) * kC + 8 * k;
-      float v[8];
+    // Tw = T diag(beta e^g) into the swizzled A tile of W, Tu = T diag(beta) to global; 16-byte
+    // chunk u: row (hh, i) = u / 8, columns 8 (u % 8) .. + 7.
+#pragma unroll 2
+    for (unsigned u = tid; u < 2 * kC * 8; u += kPrepThreads) {
+      const unsigned cc = u % 8, r = u / 8, hh = r / kC, i = r % kC;
+      const float* t = Tc + r * kC + 8 * cc;
+      const float4 ta = *reinterpret_cast<const float4*>(t);
+      const float4 tb = *reinterpret_cast<const float4*>(t + 4);
+      const float tv[8] = {ta.x, ta.y, ta.z, ta.w, tb.x, tb.y, tb.z, tb.w};
+      const float* fw = fac + (hh * 2 + 0) * kC + 8 * cc;
+      const float* fu = fac + (hh * 2 + 1) * kC + 8 * cc;
+      uint32_t w4[4], u4[4];
 #pragma unroll
-      for (int e = 0; e < 8; ++e)
-        v[e] = Tc[(hh * kC + 8 * k + e) * kTRow + i] * f[e];
+      for (int e = 0; e < 4; ++e) {
+        w4[e] = h2(tv[2 * e] * fw[2 * e], tv[2 * e + 1] * fw[2 * e + 1]);
+        u4[e] = h2(tv[2 * e] * fu[2 * e], tv[2 * e + 1] * fu[2 * e + 1]);
+      }
+      *reinterpret_cast<uint4*>(twt + dev::swz128(r, cc)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
       const unsigned h = kh + kKHeads * hh;
-      __half* dst = (which ? a.tu : a.tw) + ((size_t(h) * a.nc + c) * kC + i) * kC + 8 * k;
-      *reinterpret_cast<uint4*>(dst) =
-          make_uint4(h2(v[0], v[1]), h2(v[2], v[3]), h2(v[4], v[5]), h2(v[6], v[7]));
+      *reinterpret_cast<uint4*>(a.tu + ((size_t(h) * a.nc + c) * kC + i) * kC + 8 * cc) =
+          make_uint4(u4[0], u4[1], u4[2], u4[3]);
+    }
+    dev::fence_proxy_async_smem();
+  }
+  __syncthreads();
+  if (tid == 0 && ok) {
+    // W = [Tw_0; Tw_1] K for both V heads in one M = 128 product: A = the Tw tile (K-major,
+    // K = j), B = the K rows (MN-major, N = 128 dims in two 64-dim slabs 16 KB apart).
+    dev::tc_fence_after();
+    const uint32_t idesc = dev::idesc_f16_f32(128, 128, 0, 1);
+    const uint32_t ta = dev::smem_u32(twt);
+#pragma unroll
+    for (int kk = 0; kk < kC / 16; ++kk)
+      dev::tc_mma_f16_ss(tmem, dev::sdesc_sw128(ta + kk * 32, 16, 1024),
+                         dev::sdesc_sw128(sbase + kk * 2048, 2 * kTile, 1024), idesc, kk > 0);
+    dev::tc_commit(dev::smem_u32(&bars[2]));
+  }
+  if (ok) {
+    // Meanwhile: Ks = K rows * e^(g_last - g_j) and Qg = Q rows * e^(g_i) of both V heads, from
+    // the (unscaled) high parts. Unit u: tensor u / 1024 (K, Q), row (u / 16) % 64, 8-dim chunk
+    // u % 16 (slab chunk / 8, swizzled chunk chunk % 8).
+#pragma unroll 2
+    for (unsigned u = tid; u < 2 * kC * 16; u += kPrepThreads) {
+      const unsigned ch = u % 16, row = (u / 16) % kC, isq = u / (16 * kC);
+      const uint8_t* src = smem + (ch / 8) * 2 * kTile + isq * kTile + dev::swz128(row, ch % 8);
+      const uint4 raw = *reinterpret_cast<const uint4*>(src);
+      const __half2* hv = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const float f = (isq ? egs : egls)[hh * kC + row];
+        uint32_t o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 xv = __half22float2(hv[e]);
+          o[e] = h2(xv.x * f, xv.y * f);
+        }
+        const unsigned h = kh + kKHeads * hh;
+        __half* dst = (isq ? a.qg : a.ks) + ((size_t(h) * a.nc + c) * kC + row) * kDim + 8 * ch;
+        *reinterpret_cast<uint4*>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+  }
+  // W rows to global: thread r = (hh, i) holds row i of W_hh (TMEM lane r, 128 columns).
+  if (__all_sync(0xffffffffu, ok && dev::mbar_wait(dev::smem_u32(&bars[2]), 0, 0x31))) {
+    dev::tc_fence_after();
+    const unsigned hh = tid / kC, i = tid % kC, h = kh + kKHeads * hh;
+    uint4* dst = reinterpret_cast<uint4*>(a.w + ((size_t(h) * a.nc + c) * kC + i) * kDim);
+#pragma unroll 1
+    for (int part = 0; part < 4; ++part) {
+      uint32_t x[32];
+      dev::tmem_ld32(tmem + ((32u * warp) << 16) + 32 * part, x);
+      dev::tmem_wait_ld();
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        dst[4 * part + q] = make_uint4(
+            h2(__uint_as_float(x[8 * q]), __uint_as_float(x[8 * q + 1])),
+            h2(__uint_as_float(x[8 * q + 2]), __uint_as_float(x[8 * q + 3])),
+            h2(__uint_as_float(x[8 * q + 4]), __uint_as_float(x[8 * q + 5])),
+            h2(__uint_as_float(x[8 * q + 6]), __uint_as_float(x[8 * q + 7])));
     }
   }
   if (tid == 0 && *reinterpret_cast<volatile int*>(fail))
     dev::mbar_wait(dev::smem_u32(&bars[0]), 0, 0x31);  // let the tile copies land (bounded)
+  dev::tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     dev::tc_fence_after();
-    dev::tmem_dealloc(tmem, 64);
+    dev::tmem_dealloc(tmem, 128);
   }
 }
 
@@ -428,38 +508,30 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
 
 struct RecurArgs {
   const float* eg;      // [32][np] e^(g_t)
-  const float* egl;     // [32][np] e^(g_last - g_t)
   const float* z;       // z[t * zab_stride + h * 128 + v]
   const float* norm_w;  // [128]
   float* state;         // [32][128 k][128 v]
   float* out;           // [n][4096]
   unsigned n, np, nc, zab_stride;
-  unsigned z_prefetch;  // z rows are 16-byte aligned: the producer prefetches them into L2
   float eps;
 };
 
-constexpr int kRecurThreads = 512;  // warp 0 TMA, warp 1 MMA + TMEM, 4-11 state, 12-15 output
-// Stage (double-buffered, one chunk): K, Q as [64 tokens][128] fp16 in two 64-column boxes
-// each, Aqk high part and remainder as [64][64] fp16. The state warps scale the K rows by
-// e^(g_last - g_j) and the Q rows by e^(g_i) in place once W^T has been computed from K.
-constexpr uint32_t kStK = 0, kStQ = 2 * kTile, kStAh = 4 * kTile, kStAl = 5 * kTile,
-                   kStageBytes = 6 * kTile;  // 48 KB
-// Inputs of W^T and U^T (single-buffered, reloaded as soon as the MMAs of a chunk consumed them):
-// V high part and remainder [64][128] fp16, Tw and Tu [64][64] fp16.
+constexpr int kRecurThreads = 640;  // warp 0 TMA, warp 1 MMA + TMEM, 4-11 state, 12-19 output
+// Stage (double-buffered, one chunk), 128-byte swizzled fp16 tiles:
+//   B of the X / Y product: two 64-dim slabs of [128 rows][64], rows [W; Qg];
+//   Ks [64 j][128] as two [64][64] boxes; Aqk high part and remainder [64 i][64 j].
+constexpr uint32_t kStB = 0, kStKs = 4 * kTile, kStAh = 6 * kTile, kStAl = 7 * kTile,
+                   kStageBytes = 8 * kTile;  // 64 KB
+// U inputs (double-buffered): V high part and remainder [64 j][128] (two boxes each), Tu [64][64].
 constexpr uint32_t kOffP1 = 2 * kStageBytes;
-constexpr uint32_t kP1Vh = 0, kP1Vl = 2 * kTile, kP1Tw = 4 * kTile, kP1Tu = 5 * kTile,
-                   kP1Bytes = 6 * kTile;  // 48 KB
-constexpr uint32_t kOffS16 = kOffP1 + kP1Bytes;    // S^T fp16, two 16 KB column slabs
-constexpr uint32_t kOffW16 = kOffS16 + 4 * kTile;  // W^T fp16 [k][i] (MN-major B)
-constexpr uint32_t kOffDh = kOffW16 + 2 * kTile;   // delta^T fp16 [v][j], high part
-constexpr uint32_t kOffDl = kOffDh + 2 * kTile;    // and remainder
-constexpr uint32_t kOffRed = kOffDl + 2 * kTile;   // [2][4 warps][64] fp32
+constexpr uint32_t kP1Vh = 0, kP1Vl = 2 * kTile, kP1Tu = 4 * kTile, kP1Bytes = 5 * kTile;  // 40 KB
+constexpr uint32_t kOffRed = kOffP1 + 2 * kP1Bytes;  // [2][4 warps][64] fp32
 constexpr uint32_t kOffBar = kOffRed + 2 * 4 * kC * 4;
 
 struct RecurBars {
-  uint64_t stage_full[2], stage_empty[2], p1in_full, p1in_empty;
-  uint64_t p1_full, ut_full[2], w16_ready, kq_ready, s16_ready, s_scaled, x_full, d_ready, s_full;
-  uint64_t o_full[2], o_free[2], red_ready[2], drain;
+  uint64_t stage_full[2], stage_empty[2], p1in_full[2], p1in_empty[2];
+  uint64_t ut_full[2], s16_ready, s_scaled, x_full, d_ready, s_full;
+  uint64_t o_full, o_free, red_ready[2], drain;
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -467,8 +539,11 @@ struct RecurBars {
 constexpr size_t kRecurSmemBytes = kOffBar + sizeof(RecurBars);
 static_assert(kRecurSmemBytes <= 232448, "fits the 227 KB opt-in shared memory");
 
-// TMEM columns (lane = row of the M = 128 tiles). O and U^T are double-buffered by chunk parity.
-constexpr uint32_t kColS = 0, kColX = 128, kColO = 192, kColWt = 320, kColUt = 384;
+// TMEM columns (lane = row v of the M = 128 tiles): the fp32 state S^T, its fp16 copy (A operand
+// of X / Y, 2 values per column), [X^T | O^T] (one N = 128 accumulator), delta^T high part and
+// remainder (A operands of the S and O updates), U^T of even and odd chunks.
+constexpr uint32_t kColS = 0, kColS16 = 128, kColX = 192, kColO = 256, kColDh = 320,
+                   kColDl = 352, kColUt = 384;
 
 __device__ __forceinline__ bool aborted(const RecurBars& b) {
   return *reinterpret_cast<const volatile int*>(&b.abort_flag) != 0;
@@ -484,6 +559,29 @@ __device__ __forceinline__ bool wait_or_abort(RecurBars& b, uint64_t& bar, uint3
   return true;
 }
 
+// Single-thread bounded wait that polls the barrier (mbarrier.test_wait) instead of suspending in
+// try_wait: the MMA issuer resumes as soon as the phase completes, not when the suspended wait is
+// next rescheduled.
+__device__ __forceinline__ bool poll_or_abort(RecurBars& b, uint64_t& bar, uint32_t parity) {
+  const uint32_t a = dev::smem_u32(&bar);
+  if (dev::mbar_test_wait(a, parity))
+    return true;
+  const long long t0 = clock64();
+  for (unsigned i = 1;; ++i) {
+    if (dev::mbar_test_wait(a, parity))
+      return true;
+    if ((i & 63u) == 0) {
+      if (aborted(b))
+        return false;
+      if (clock64() - t0 > dev::kWaitLimitCycles) {
+        dev::set_status(dev::kStatusTimeout, 0x30);
+        b.abort_flag = 1;
+        return false;
+      }
+    }
+  }
+}
+
 // Warp-collective bounded wait: every lane waits, the warp proceeds only if all succeeded.
 __device__ __forceinline__ bool warp_wait(RecurBars& b, uint64_t& bar, uint32_t parity) {
   return __all_sync(0xffffffffu, wait_or_abort(b, bar, parity));
@@ -495,37 +593,18 @@ __device__ __forceinline__ void warp_arrive(uint64_t& bar) {
     dev::mbar_arrive(dev::smem_u32(&bar));
 }
 
-// Eight fp32 values as one 16-byte chunk of fp16.
-__device__ __forceinline__ uint4 pack8(const float* v) {
-  return make_uint4(h2(v[0], v[1]), h2(v[2], v[3]), h2(v[4], v[5]), h2(v[6], v[7]));
-}
-
-// Eight fp32 values as fp16 high parts and remainders (two 16-byte chunks).
-__device__ __forceinline__ void split8(const float* v, uint4& hi, uint4& lo) {
-  uint2 h0, l0, h1, l1;
-  const float a[4] = {v[0], v[1], v[2], v[3]}, b[4] = {v[4], v[5], v[6], v[7]};
-  split4(a, h0, l0);
-  split4(b, h1, l1);
-  hi = make_uint4(h0.x, h0.y, h1.x, h1.y);
-  lo = make_uint4(l0.x, l0.y, l1.x, l1.y);
-}
-
-// Scales the eight fp16 values of a 16-byte chunk by f (in place).
-__device__ __forceinline__ void scale8(uint4* p, float f) {
-  uint4 w = *p;
-  __half2* h = reinterpret_cast<__half2*>(&w);
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const float2 x = __half22float2(h[e]);
-    h[e] = __floats2half2_rn(x.x * f, x.y * f);
-  }
-  *p = w;
+// Two fp32 values as fp16 high parts (one packed pair) and remainders (another pair).
+__device__ __forceinline__ void split2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  const __half2 hv = __floats2half2_rn(x0, x1);
+  const float2 f = __half22float2(hv);
+  hi = *reinterpret_cast<const uint32_t*>(&hv);
+  lo = h2(x0 - f.x, x1 - f.y);
 }
 
 __global__ void __launch_bounds__(kRecurThreads, 1)
-    recur_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
-                 const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap vlmap,
-                 const __grid_constant__ CUtensorMap twmap, const __grid_constant__ CUtensorMap tumap,
+    recur_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap qgmap,
+                 const __grid_constant__ CUtensorMap ksmap, const __grid_constant__ CUtensorMap vmap,
+                 const __grid_constant__ CUtensorMap vlmap, const __grid_constant__ CUtensorMap tumap,
                  const __grid_constant__ CUtensorMap aqkmap,
                  const __grid_constant__ CUtensorMap aqklmap, RecurArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -535,26 +614,22 @@ __global__ void __launch_bounds__(kRecurThreads, 1)
     return;
   }
   RecurBars& bar = *reinterpret_cast<RecurBars*>(smem + kOffBar);
-  const unsigned h = blockIdx.x, kh = h % kKHeads, warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const unsigned h = blockIdx.x, warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const unsigned nc = a.nc;
   const uint32_t sbase = dev::smem_u32(smem);
   const float* egh = a.eg + size_t(h) * a.np;
-  const float* eglh = a.egl + size_t(h) * a.np;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < 2; ++s) {
       dev::mbar_init(dev::smem_u32(&bar.stage_full[s]), 1);
       dev::mbar_init(dev::smem_u32(&bar.stage_empty[s]), 1);
+      dev::mbar_init(dev::smem_u32(&bar.p1in_full[s]), 1);
+      dev::mbar_init(dev::smem_u32(&bar.p1in_empty[s]), 1);
       dev::mbar_init(dev::smem_u32(&bar.ut_full[s]), 1);
-      dev::mbar_init(dev::smem_u32(&bar.o_full[s]), 1);
-      dev::mbar_init(dev::smem_u32(&bar.o_free[s]), 4);
-      dev::mbar_init(dev::smem_u32(&bar.red_ready[s]), 4);
+      dev::mbar_init(dev::smem_u32(&bar.red_ready[s]), 8);
     }
-    dev::mbar_init(dev::smem_u32(&bar.p1in_full), 1);
-    dev::mbar_init(dev::smem_u32(&bar.p1in_empty), 1);
-    dev::mbar_init(dev::smem_u32(&bar.p1_full), 1);
-    dev::mbar_init(dev::smem_u32(&bar.w16_ready), 8);
-    dev::mbar_init(dev::smem_u32(&bar.kq_ready), 8);
+    dev::mbar_init(dev::smem_u32(&bar.o_full), 1);
+    dev::mbar_init(dev::smem_u32(&bar.o_free), 8);
     dev::mbar_init(dev::smem_u32(&bar.s16_ready), 8);
     dev::mbar_init(dev::smem_u32(&bar.s_scaled), 8);
     dev::mbar_init(dev::smem_u32(&bar.x_full), 1);
@@ -576,219 +651,162 @@ __global__ void __launch_bounds__(kRecurThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------------------------ producer
     if (lane == 0) {
-      dev::tma_prefetch_desc(&qmap);
-      dev::tma_prefetch_desc(&kmap);
+      dev::tma_prefetch_desc(&wmap);
+      dev::tma_prefetch_desc(&qgmap);
       dev::tma_prefetch_desc(&vmap);
-      unsigned staged = 0, p1in = 0;  // chunks whose stage / W-U inputs have been issued
+      unsigned staged = 0, p1in = 0;  // chunks whose stage / U inputs have been issued
       for (unsigned c = 0; c < nc; ++c) {
         const unsigned s = c & 1;
-        if (c >= 2 && !wait_or_abort(bar, bar.stage_empty[s], ((c >> 1) & 1) ^ 1))
-          break;
-        const uint32_t sb = sbase + s * kStageBytes, full = dev::smem_u32(&bar.stage_full[s]);
-        dev::mbar_arrive_expect_tx(full, kStageBytes);
-        for (int x = 0; x < 2; ++x) {
-          dev::tma_load_3d(sb + kStK + x * kTile, &kmap, x * 64, kh, c * kC, full);
-          dev::tma_load_3d(sb + kStQ + x * kTile, &qmap, x * 64, kh, c * kC, full);
-        }
         const int row = int((h * nc + c) * kC);
-        dev::tma_load_2d(sb + kStAh, &aqkmap, 0, row, full);
-        dev::tma_load_2d(sb + kStAl, &aqklmap, 0, row, full);
-        staged = c + 1;
-        if (c >= 1 && !wait_or_abort(bar, bar.p1in_empty, (c - 1) & 1))
+        if (c >= 2 && !wait_or_abort(bar, bar.p1in_empty[s], ((c >> 1) & 1) ^ 1))
           break;
-        const uint32_t pb = sbase + kOffP1, pfull = dev::smem_u32(&bar.p1in_full);
+        const uint32_t pb = sbase + kOffP1 + s * kP1Bytes, pfull = dev::smem_u32(&bar.p1in_full[s]);
         dev::mbar_arrive_expect_tx(pfull, kP1Bytes);
         for (int x = 0; x < 2; ++x) {
           dev::tma_load_3d(pb + kP1Vh + x * kTile, &vmap, x * 64, h, c * kC, pfull);
           dev::tma_load_3d(pb + kP1Vl + x * kTile, &vlmap, x * 64, h, c * kC, pfull);
         }
-        dev::tma_load_2d(pb + kP1Tw, &twmap, 0, row, pfull);
         dev::tma_load_2d(pb + kP1Tu, &tumap, 0, row, pfull);
         p1in = c + 1;
-        if (a.z_prefetch) {  // this chunk's gate rows (512 B each) into L2 for the output warps
-          for (unsigned i = 0; i < kC && c * kC + i < a.n; ++i)
-            dev::prefetch_l2(a.z + size_t(c * kC + i) * a.zab_stride + h * kDim, kDim * 4);
+        if (c >= 2 && !wait_or_abort(bar, bar.stage_empty[s], ((c >> 1) & 1) ^ 1))
+          break;
+        const uint32_t sb = sbase + s * kStageBytes, full = dev::smem_u32(&bar.stage_full[s]);
+        dev::mbar_arrive_expect_tx(full, kStageBytes);
+        for (int x = 0; x < 2; ++x) {
+          dev::tma_load_2d(sb + kStB + x * 2 * kTile, &wmap, x * 64, row, full);
+          dev::tma_load_2d(sb + kStB + x * 2 * kTile + kTile, &qgmap, x * 64, row, full);
+          dev::tma_load_2d(sb + kStKs + x * kTile, &ksmap, x * 64, row, full);
         }
+        dev::tma_load_2d(sb + kStAh, &aqkmap, 0, row, full);
+        dev::tma_load_2d(sb + kStAl, &aqklmap, 0, row, full);
+        staged = c + 1;
       }
       if (aborted(bar)) {  // let the copies already issued land before the CTA exits (bounded)
         for (unsigned c = staged >= 2 ? staged - 2 : 0; c < staged; ++c)
           dev::mbar_wait(dev::smem_u32(&bar.stage_full[c & 1]), (c >> 1) & 1);
-        if (p1in > 0)
-          dev::mbar_wait(dev::smem_u32(&bar.p1in_full), (p1in - 1) & 1);
+        for (unsigned c = p1in >= 2 ? p1in - 2 : 0; c < p1in; ++c)
+          dev::mbar_wait(dev::smem_u32(&bar.p1in_full[c & 1]), (c >> 1) & 1);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------------------ MMA issue
+    // Per chunk c, in issue order (the tensor pipe runs them in order):
+    //   XY(c)    [X^T | O^T] = S16 [W; Qg]^T (N = 128)   after E0(c) wrote S16, O^T(c-1) was read
+    //   U(c+1)   U^T = (V_hi + V_lo)^T Tu^T             (double-buffered; runs during E1(c))
+    //   C2(c)    S^T += Dh Ks                          after E1(c): delta written, S scaled
+    //   Z(c)     O^T += Dh Ah + Dh Al + Dl Ah          (runs during E0(c+1))
+    // so the tensor pipe works on U while the state warps form delta, and on Z while they copy
+    // the next state, and the chain E0 -> XY -> E1 -> C2 -> E0 never queues behind them.
     if (lane == 0) {
-      const uint32_t id_x = dev::idesc_f16_f32(128, 64, 0, 1);   // S^T . W^T   (B MN-major)
-      const uint32_t id_y = dev::idesc_f16_f32(128, 64, 0, 0);   // S^T . Qg^T
-      const uint32_t id_p = dev::idesc_f16_f32(128, 64, 1, 0);   // K^T . Tw^T  (A MN-major)
-      const uint32_t id_s = dev::idesc_f16_f32(128, 128, 0, 1);  // delta^T . Ks
-      const uint32_t id_z = dev::idesc_f16_f32(128, 64, 0, 0);   // delta^T . Aqk^T
+      const uint32_t id_xy = dev::idesc_f16_f32(128, 128, 0, 0);  // A (TMEM) . B K-major
+      const uint32_t id_s = dev::idesc_f16_f32(128, 128, 0, 1);   // A (TMEM) . Ks MN-major
+      const uint32_t id_z = dev::idesc_f16_f32(128, 64, 0, 0);    // A (TMEM) . Aqk K-major
+      const uint32_t id_u = dev::idesc_f16_f32(128, 64, 1, 0);    // V^T MN-major . Tu K-major
       auto kdesc = [](uint32_t addr) { return dev::sdesc_sw128(addr, 16, 1024); };
       auto mdesc = [](uint32_t addr) { return dev::sdesc_sw128(addr, kTile, 1024); };
-      // W^T = K^T Tw^T and U^T = (V_hi + V_lo)^T Tu^T of chunk c.
-      auto issue_p1 = [&](unsigned c) {
-        const uint32_t sb = sbase + (c & 1) * kStageBytes, pb = sbase + kOffP1;
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          dev::tc_mma_f16_ss(tmem + kColWt, mdesc(sb + kStK + kk * 2048),
-                             kdesc(pb + kP1Tw + kk * 32), id_p, kk > 0);
+      auto issue_u = [&](unsigned c) {
+        const uint32_t pb = sbase + kOffP1 + (c & 1) * kP1Bytes;
 #pragma unroll
         for (int t = 0; t < 2; ++t)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
             dev::tc_mma_f16_ss(tmem + kColUt + 64 * (c & 1),
                                mdesc(pb + (t ? kP1Vl : kP1Vh) + kk * 2048),
-                               kdesc(pb + kP1Tu + kk * 32), id_p, (t | kk) != 0);
-        dev::tc_commit(dev::smem_u32(&bar.p1_full));
+                               kdesc(pb + kP1Tu + kk * 32), id_u, (t | kk) != 0);
         dev::tc_commit(dev::smem_u32(&bar.ut_full[c & 1]));
-        dev::tc_commit(dev::smem_u32(&bar.p1in_empty));
+        dev::tc_commit(dev::smem_u32(&bar.p1in_empty[c & 1]));
       };
-      bool ok = wait_or_abort(bar, bar.stage_full[0], 0) && wait_or_abort(bar, bar.p1in_full, 0);
+      bool ok = poll_or_abort(bar, bar.p1in_full[0], 0);
       if (ok) {
         dev::tc_fence_after();
-        issue_p1(0);
+        issue_u(0);
       }
       for (unsigned c = 0; ok && c < nc; ++c) {
         const unsigned b = c & 1;
-        const uint32_t sb = sbase + b * kStageBytes, ocol = tmem + kColO + 64 * b;
-        if (!wait_or_abort(bar, bar.s16_ready, c & 1) || !wait_or_abort(bar, bar.w16_ready, c & 1))
+        const uint32_t sb = sbase + b * kStageBytes;
+        if (!poll_or_abort(bar, bar.stage_full[b], (c >> 1) & 1) ||
+            !poll_or_abort(bar, bar.s16_ready, c & 1) ||
+            (c >= 1 && !poll_or_abort(bar, bar.o_free, (c - 1) & 1)))
           break;
         dev::tc_fence_after();
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks)
-          dev::tc_mma_f16_ss(tmem + kColX,
-                             kdesc(sbase + kOffS16 + (ks >> 2) * 2 * kTile + (ks & 3) * 32),
-                             mdesc(sbase + kOffW16 + ks * 2048), id_x, ks > 0);
+          dev::tc_mma_f16_ts(tmem + kColX, tmem + kColS16 + 8 * ks,
+                             kdesc(sb + kStB + (ks >> 2) * 2 * kTile + (ks & 3) * 32), id_xy,
+                             ks > 0);
         dev::tc_commit(dev::smem_u32(&bar.x_full));
-        // The scaled K / Q of this chunk (and W^T read from the unscaled K) must be in place
-        // before the next chunk's W^T / U^T are issued, so that the state warps' next kq_ready
-        // arrival cannot run ahead of this wait.
-        if (!wait_or_abort(bar, bar.kq_ready, c & 1))
-          break;
         if (c + 1 < nc) {
-          if (!wait_or_abort(bar, bar.stage_full[(c + 1) & 1], ((c + 1) >> 1) & 1) ||
-              !wait_or_abort(bar, bar.p1in_full, (c + 1) & 1))
+          if (!poll_or_abort(bar, bar.p1in_full[(c + 1) & 1], ((c + 1) >> 1) & 1))
             break;
           dev::tc_fence_after();
-          issue_p1(c + 1);
+          issue_u(c + 1);
         }
-        if (c >= 2 && !wait_or_abort(bar, bar.o_free[b], ((c >> 1) & 1) ^ 1))
-          break;
-        dev::tc_fence_after();
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks)
-          dev::tc_mma_f16_ss(ocol, kdesc(sbase + kOffS16 + (ks >> 2) * 2 * kTile + (ks & 3) * 32),
-                             kdesc(sb + kStQ + (ks >> 2) * kTile + (ks & 3) * 32), id_y, ks > 0);
-        if (!wait_or_abort(bar, bar.d_ready, c & 1) || !wait_or_abort(bar, bar.s_scaled, c & 1))
+        if (!poll_or_abort(bar, bar.d_ready, c & 1) || !poll_or_abort(bar, bar.s_scaled, c & 1))
           break;
         dev::tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-          dev::tc_mma_f16_ss(tmem + kColS, kdesc(sbase + kOffDh + kk * 32),
-                             mdesc(sb + kStK + kk * 2048), id_s, 1);
+          dev::tc_mma_f16_ts(tmem + kColS, tmem + kColDh + 8 * kk, mdesc(sb + kStKs + kk * 2048),
+                             id_s, 1);
         dev::tc_commit(dev::smem_u32(&bar.s_full));
         // O += D_hi A_hi + D_hi A_lo + D_lo A_hi
-        const uint32_t za[3] = {kOffDh, kOffDh, kOffDl}, zb[3] = {kStAh, kStAl, kStAh};
+        const uint32_t za[3] = {kColDh, kColDh, kColDl}, zb[3] = {kStAh, kStAl, kStAh};
 #pragma unroll
         for (int t = 0; t < 3; ++t)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            dev::tc_mma_f16_ss(ocol, kdesc(sbase + za[t] + kk * 32), kdesc(sb + zb[t] + kk * 32),
+            dev::tc_mma_f16_ts(tmem + kColO, tmem + za[t] + 8 * kk, kdesc(sb + zb[t] + kk * 32),
                                id_z, 1);
-        dev::tc_commit(dev::smem_u32(&bar.o_full[b]));
+        dev::tc_commit(dev::smem_u32(&bar.o_full));
         dev::tc_commit(dev::smem_u32(&bar.stage_empty[b]));
       }
       dev::tc_commit(dev::smem_u32(&bar.drain));
       dev::mbar_wait(dev::smem_u32(&bar.drain), 0);
     }
   } else if (warp >= 4 && warp < 12) {
-    // ------------------------------- state warps: S^T copies, delta^T, W^T to fp16, K / Q scaling
-    // Warp (4 + q + 4 hc): TMEM lanes [32 q, 32 q + 32) (rows v of S^T, X, U; rows k of W^T);
-    // S^T columns (k) [64 hc, +64), X / U / W^T columns [32 hc, +32).
+    // ------------------------------------------------------ state warps: S16, S decay, delta
+    // Warp (4 + q + 4 hc): TMEM lanes [32 q, 32 q + 32) (rows v), S^T columns (k) [64 hc, +64),
+    // X^T / U^T columns (i) [32 hc, +32).
     const unsigned q = warp & 3, hc = (warp - 4) >> 2, v = 32 * q + lane;
-    const unsigned st = threadIdx.x - 128;  // 0..255
     const uint32_t trow = tmem + ((32u * q) << 16);
-    uint8_t* s16 = smem + kOffS16 + hc * 2 * kTile + v * 128;
-    uint8_t* dh16 = smem + kOffDh + v * 128;
-    uint8_t* dl16 = smem + kOffDl + v * 128;
-    uint8_t* w16 = smem + kOffW16 + v * 128;  // row k = v of W^T
     const float* S = a.state + size_t(h) * kDim * kDim;
-    // EW(c): W^T of chunk c (TMEM, fp32) -> fp16 rows [k][i] of W16, the MN-major B operand of
-    // X(c); then, W^T having consumed the unscaled K, the K rows of the stage are scaled by
-    // e^(g_last - g_j) (the state update's decay) and the Q rows by e^(g_i) (the output's).
-    // W16 is free: X(c - 1) has completed (E1(c - 1) waited for it).
-    auto ew = [&](unsigned c) -> bool {
-      const unsigned r0 = st / 8, r1 = r0 + 32;  // the two tile rows this thread rescales
-      const float fk0 = eglh[c * kC + r0], fk1 = eglh[c * kC + r1];
-      const float fq0 = egh[c * kC + r0], fq1 = egh[c * kC + r1];
-      if (!warp_wait(bar, bar.p1_full, c & 1) ||
-          !warp_wait(bar, bar.stage_full[c & 1], (c >> 1) & 1))
-        return false;
-      dev::tc_fence_after();
-      uint32_t x[32];
-      dev::tmem_ld32(trow + kColWt + 32 * hc, x);
-      dev::tmem_wait_ld();
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        float f[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e)
-          f[e] = __uint_as_float(x[8 * cc + e]);
-        *reinterpret_cast<uint4*>(w16 + (((4 * hc + cc) ^ (v & 7)) << 4)) = pack8(f);
-      }
-      dev::fence_proxy_async_smem();
-      dev::tc_fence_before();
-      warp_arrive(bar.w16_ready);
-      // 16-byte chunk u = st + 256 m of a [64 rows][128 B] x 2 box tile lies in row (u % 512) / 8.
-      uint4* kt = reinterpret_cast<uint4*>(smem + (c & 1) * kStageBytes + kStK);
-      uint4* qt = reinterpret_cast<uint4*>(smem + (c & 1) * kStageBytes + kStQ);
-#pragma unroll
-      for (int m = 0; m < 4; ++m) {
-        scale8(kt + st + 256 * m, (m & 1) ? fk1 : fk0);
-        scale8(qt + st + 256 * m, (m & 1) ? fq1 : fq0);
-      }
-      dev::fence_proxy_async_smem();
-      warp_arrive(bar.kq_ready);
-      return true;
-    };
-    bool ok = ew(0);
+    bool ok = true;
     for (unsigned c = 0; ok && c < nc; ++c) {
       const float el = egh[c * kC + kC - 1];  // e^(g_last)
-      // E0: fp16 copy of S^T for X / Y, then S^T *= e^(g_last) in TMEM for the update MMA.
+      // E0: fp16 copy of S^T (the A operand of XY), then S^T *= e^(g_last) for the update.
       if (c > 0 && !warp_wait(bar, bar.s_full, (c - 1) & 1)) {
         ok = false;
         break;
       }
       dev::tc_fence_after();
-#pragma unroll 1
-      for (int half = 0; half < 2; ++half) {
-        const uint32_t col = kColS + 64 * hc + 32 * half;
-        uint32_t x[32];
-        if (c == 0) {
+      uint32_t x[64];
+      uint32_t (&x0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&x[0]);
+      uint32_t (&x1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&x[32]);
+      if (c == 0) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e)
-            x[e] = __float_as_uint(S[size_t(64 * hc + 32 * half + e) * kDim + v]);
-        } else {
-          dev::tmem_ld32(trow + col, x);
-          dev::tmem_wait_ld();
-        }
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          float f[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e)
-            f[e] = __uint_as_float(x[8 * cc + e]);
-          *reinterpret_cast<uint4*>(s16 + (((4 * half + cc) ^ (v & 7)) << 4)) = pack8(f);
-        }
-#pragma unroll
-        for (int e = 0; e < 32; ++e)
-          x[e] = __float_as_uint(__uint_as_float(x[e]) * el);
-        dev::tmem_st32(trow + col, x);
+        for (int e = 0; e < 64; ++e)
+          x[e] = __float_as_uint(S[size_t(64 * hc + e) * kDim + v]);
+      } else {
+        dev::tmem_ld32(trow + kColS + 64 * hc, x0);
+        dev::tmem_ld32(trow + kColS + 64 * hc + 32, x1);
+        dev::tmem_wait_ld();
       }
-      dev::fence_proxy_async_smem();
+#pragma unroll
+      for (int part = 0; part < 2; ++part) {
+        uint32_t p16[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          p16[e] = h2(__uint_as_float(x[32 * part + 2 * e]), __uint_as_float(x[32 * part + 2 * e + 1]));
+        dev::tmem_st16(trow + kColS16 + 32 * hc + 16 * part, p16);
+      }
+      dev::tmem_wait_st();
+      dev::tc_fence_before();
       warp_arrive(bar.s16_ready);
+#pragma unroll
+      for (int e = 0; e < 64; ++e)
+        x[e] = __float_as_uint(__uint_as_float(x[e]) * el);
+      dev::tmem_st32(trow + kColS + 64 * hc, x0);
+      dev::tmem_st32(trow + kColS + 64 * hc + 32, x1);
       dev::tmem_wait_st();
       dev::tc_fence_before();
       warp_arrive(bar.s_scaled);
@@ -805,24 +823,20 @@ __global__ void __launch_bounds__(kRecurThreads, 1)
       dev::tmem_ld32(trow + kColUt + 64 * (c & 1) + 32 * hc, uu);
       dev::tmem_wait_ld();
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        float d[8];
+      for (int part = 0; part < 2; ++part) {
+        uint32_t dh[8], dl[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e)
-          d[e] = __uint_as_float(uu[8 * cc + e]) - __uint_as_float(xx[8 * cc + e]);
-        uint4 hi, lo;
-        split8(d, hi, lo);
-        const unsigned chunk = ((4 * hc + cc) ^ (v & 7)) << 4;
-        *reinterpret_cast<uint4*>(dh16 + chunk) = hi;
-        *reinterpret_cast<uint4*>(dl16 + chunk) = lo;
+        for (int e = 0; e < 8; ++e) {
+          const int i = 16 * part + 2 * e;
+          split2(__uint_as_float(uu[i]) - __uint_as_float(xx[i]),
+                 __uint_as_float(uu[i + 1]) - __uint_as_float(xx[i + 1]), dh[e], dl[e]);
+        }
+        dev::tmem_st8(trow + kColDh + 16 * hc + 8 * part, dh);
+        dev::tmem_st8(trow + kColDl + 16 * hc + 8 * part, dl);
       }
-      dev::fence_proxy_async_smem();
+      dev::tmem_wait_st();
       dev::tc_fence_before();
       warp_arrive(bar.d_ready);
-      if (c + 1 < nc && !ew(c + 1)) {
-        ok = false;
-        break;
-      }
     }
     // Final state back to [k][v] (coalesced over v).
     if (ok && warp_wait(bar, bar.s_full, (nc - 1) & 1)) {
@@ -840,40 +854,43 @@ __global__ void __launch_bounds__(kRecurThreads, 1)
     }
   } else if (warp >= 12) {
     // ------------------------------------------------ output warps: RMS norm, gate, store
-    // Thread = value column v of the head. O^T[v][i] of chunk c is read from TMEM twice: once for
-    // the sums of squares (reduced over v), then eight tokens at a time for the outputs. The 64
-    // gate inputs of the chunk are loaded before O is waited for, and the per-token arithmetic
-    // is branch-free (one warp-uniform bound check per group of eight), so the dependent
-    // latencies of the eight tokens overlap.
-    const unsigned q = warp & 3, v = 32 * q + lane;
+    // Two warps per TMEM lane quadrant: warp (12 + q + 4 oh) owns value column v = 32 q + lane
+    // of the head and tokens [32 oh, 32 oh + 32) of each chunk. Its 32 O^T values are read from
+    // TMEM once; the sums of squares over v are reduced across the warp by shuffles and across
+    // the four quadrants through shared memory. The 32 gate inputs are loaded before O is waited
+    // for, and the per-token arithmetic is branch-free (one warp-uniform bound check per group
+    // of eight tokens).
+    const unsigned q = warp & 3, oh = (warp - 12) >> 2, v = 32 * q + lane;
     const uint32_t trow = tmem + ((32u * q) << 16);
     float* red = reinterpret_cast<float*>(smem + kOffRed);
     const float nw = a.norm_w[v];
     const float* zh = a.z + h * kDim + v;
-    float* oh = a.out + h * kDim + v;
-    constexpr int kG = 8;
+    float* out_v = a.out + h * kDim + v;
+    constexpr int kG = 8, kT = 32;
     for (unsigned c = 0; c < nc; ++c) {
-      const unsigned b = c & 1, t0 = c * kC;
-      const uint32_t ocol = trow + kColO + 64 * b;
-      const unsigned last = a.n - 1 - t0;  // tokens past the end read token n - 1's gate (unused)
-      float zr[kC];
+      const unsigned b = c & 1, t0 = c * kC + kT * oh;
+      const uint32_t ocol = trow + kColO + kT * oh;
+      // Tokens past the end read the last token's gate (their outputs are not stored).
+      float zr[kT];
 #pragma unroll
-      for (int i = 0; i < kC; ++i)
-        zr[i] = zh[size_t(t0 + min(unsigned(i), last)) * a.zab_stride];
-      if (!warp_wait(bar, bar.o_full[b], (c >> 1) & 1))
+      for (int i = 0; i < kT; ++i)
+        zr[i] = zh[size_t(min(t0 + unsigned(i), a.n - 1)) * a.zab_stride];
+      if (!warp_wait(bar, bar.o_full, c & 1))
         break;
       dev::tc_fence_after();
+      uint32_t x[kT];
+      dev::tmem_ld32(ocol, x);
+      dev::tmem_wait_ld();
+      // O is in registers: release the TMEM columns to the next chunk's products now.
+      dev::tc_fence_before();
+      warp_arrive(bar.o_free);
       float* rb = red + b * 4 * kC;
-#pragma unroll 1
-      for (int half = 0; half < 2; ++half) {
-        uint32_t x[32];
-        dev::tmem_ld32(ocol + 32 * half, x);
-        dev::tmem_wait_ld();
-        float s2[32];
+      {
+        float s2[kT];
 #pragma unroll
-        for (int e = 0; e < 32; ++e)
+        for (int e = 0; e < kT; ++e)
           s2[e] = __uint_as_float(x[e]) * __uint_as_float(x[e]);
-        // Reduce-scatter over the warp: lane l ends with token 32 half + l.
+        // Reduce-scatter over the warp: lane l ends with token kT oh + l.
 #pragma unroll
         for (int off = 16; off >= 1; off >>= 1) {
           const bool upper = (lane & off) != 0;
@@ -884,7 +901,7 @@ __global__ void __launch_bounds__(kRecurThreads, 1)
             s2[k] = keep + __shfl_xor_sync(0xffffffffu, send, off);
           }
         }
-        rb[q * kC + 32 * half + lane] = s2[0];
+        rb[q * kC + kT * oh + lane] = s2[0];
       }
       // Exchange through an mbarrier (bounded wait), so a warp that gave up cannot strand the
       // others. Buffer b is rewritten only after every warp has passed the next chunk's wait,
@@ -892,24 +909,19 @@ __global__ void __launch_bounds__(kRecurThreads, 1)
       warp_arrive(bar.red_ready[b]);
       if (!warp_wait(bar, bar.red_ready[b], (c >> 1) & 1))
         break;
-      // 1 / rms of tokens lane and 32 + lane, shared across the warp by shuffles below.
-      const float r_lo = rsqrtf((rb[lane] + rb[kC + lane] + rb[2 * kC + lane] + rb[3 * kC + lane]) *
-                                    (1.0f / kDim) + a.eps);
-      const float r_hi = rsqrtf((rb[32 + lane] + rb[kC + 32 + lane] + rb[2 * kC + 32 + lane] +
-                                 rb[3 * kC + 32 + lane]) * (1.0f / kDim) + a.eps);
+      const unsigned ti = kT * oh + lane;
+      const float r_own = rsqrtf((rb[ti] + rb[kC + ti] + rb[2 * kC + ti] + rb[3 * kC + ti]) *
+                                     (1.0f / kDim) + a.eps);
 #pragma unroll
-      for (int g = 0; g < kC / kG; ++g) {
-        uint32_t x[kG];
-        dev::tmem_ld8(ocol + kG * g, x);
-        dev::tmem_wait_ld();
+      for (int g = 0; g < kT / kG; ++g) {
         float y[kG];
 #pragma unroll
         for (int e = 0; e < kG; ++e) {
           const int i = kG * g + e;
-          const float r = __shfl_sync(0xffffffffu, i < 32 ? r_lo : r_hi, i & 31);
-          y[e] = __uint_as_float(x[e]) * r * nw * silu_fast(zr[i]);
+          const float r = __shfl_sync(0xffffffffu, r_own, i);
+          y[e] = __uint_as_float(x[i]) * r * nw * silu_fast(zr[i]);
         }
-        float* dst = oh + size_t(t0 + kG * g) * kVHeads * kDim;
+        float* dst = out_v + size_t(t0 + kG * g) * kVHeads * kDim;
         if (t0 + kG * g + kG <= a.n) {
 #pragma unroll
           for (int e = 0; e < kG; ++e)
@@ -921,8 +933,6 @@ __global__ void __launch_bounds__(kRecurThreads, 1)
               dst[size_t(e) * kVHeads * kDim] = y[e];
         }
       }
-      dev::tc_fence_before();
-      warp_arrive(bar.o_free[b]);
     }
   }
 
