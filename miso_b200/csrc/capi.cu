@@ -637,10 +637,6 @@ int miso_deltanet_prefill_tc(const miso_deltanet_seq_params* p, void* scratch, s
   ca.np = np;
   ca.qkv_stride = p->qkv_stride;
   ca.zab_stride = p->zab_stride;
-  dc::conv_kernel<<<dim3(8, (p->n + dc::kConvTokens - 1) / dc::kConvTokens), dc::kConvThreads, 0,
-                    s>>>(ca);
-  if ((st = launch_status()) != MISO_OK)
-    return st;
 
   dc::PrepareArgs pa;
   pa.beta = beta;
@@ -655,10 +651,6 @@ int miso_deltanet_prefill_tc(const miso_deltanet_seq_params* p, void* scratch, s
   pa.n = p->n;
   pa.np = np;
   pa.nc = nc;
-  dc::prepare_kernel<<<dim3(nc, 16), dc::kPrepThreads, dc::kPrepSmemBytes, s>>>(qmap, kmap, qlmap,
-                                                                                 klmap, pa);
-  if ((st = launch_status()) != MISO_OK)
-    return st;
 
   dc::RecurArgs ra;
   ra.eg = eg;
@@ -671,6 +663,23 @@ int miso_deltanet_prefill_tc(const miso_deltanet_seq_params* p, void* scratch, s
   ra.nc = nc;
   ra.zab_stride = p->zab_stride;
   ra.eps = p->eps;
+
+  // Three launches in stream order. (Overlapping the prepare kernel of later chunks with the
+  // recurrence of earlier ones on a second stream was measured slower: the recurrence is
+  // latency-bound and slows down next to other kernels, and every extra launch of it refills
+  // its pipeline.)
+  ca.t_begin = 0;
+  dc::conv_kernel<<<dim3(8, (p->n + dc::kConvTokens - 1) / dc::kConvTokens), dc::kConvThreads, 0,
+                    s>>>(ca);
+  if ((st = launch_status()) != MISO_OK)
+    return st;
+  pa.c_begin = 0;
+  dc::prepare_kernel<<<dim3(nc, 16), dc::kPrepThreads, dc::kPrepSmemBytes, s>>>(qmap, kmap, qlmap,
+                                                                                 klmap, pa);
+  if ((st = launch_status()) != MISO_OK)
+    return st;
+  ra.c_begin = 0;
+  ra.c_end = nc;
   dc::recur_kernel<<<32, dc::kRecurThreads, dc::kRecurSmemBytes, s>>>(
       wmap, qgmap, ksmap, vmap, vlmap, tumap, aqkmap, aqklmap, ra);
   return launch_status();

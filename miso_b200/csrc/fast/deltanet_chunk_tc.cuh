@@ -96,6 +96,7 @@ struct ConvArgs {
   float* beta;  // [32][np]
   float* loga;  // [32][np]
   unsigned n, np, qkv_stride, zab_stride;
+  unsigned t_begin;  // first token of this launch (a multiple of 16; the grid covers the rest)
 };
 
 constexpr int kConvThreads = 256;
@@ -106,7 +107,7 @@ constexpr int kConvTokens = 16;  // tokens per block: the block's conv weights a
 // heads; 2, 3: k heads; 4..7: v heads) and the q / k L2 norms are warp reductions. The 4-tap
 // window slides along the block's tokens in registers.
 __global__ void __launch_bounds__(kConvThreads) conv_kernel(ConvArgs a) {
-  const unsigned m = blockIdx.x, t0 = blockIdx.y * kConvTokens, tid = threadIdx.x,
+  const unsigned m = blockIdx.x, t0 = a.t_begin + blockIdx.y * kConvTokens, tid = threadIdx.x,
                  lane = tid % 32, warp = tid / 32;
   const unsigned c = 1024 * m + 4 * tid;
   const float4* w4 = reinterpret_cast<const float4*>(a.conv_w + 4 * size_t(c));
@@ -206,6 +207,7 @@ struct PrepareArgs {
   __half* aqk;        // [32][nc][64][64] Aqk as fp16 high part ...
   __half* aqklo;      // ... and fp16 remainder
   unsigned n, np, nc;
+  unsigned c_begin;  // first chunk of this launch (block x = chunk - c_begin)
 };
 
 constexpr int kPrepThreads = 128;
@@ -231,7 +233,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2)
       dev::set_status(dev::kStatusTimeout, 0x31);
     return;
   }
-  const unsigned c = blockIdx.x, kh = blockIdx.y, tid = threadIdx.x, warp = tid / 32,
+  const unsigned c = a.c_begin + blockIdx.x, kh = blockIdx.y, tid = threadIdx.x, warp = tid / 32,
                  lane = tid % 32;
   const uint32_t sbase = dev::smem_u32(smem);
   float* Ls = reinterpret_cast<float*>(smem + kPrepOffL);  // [2][64][kLRow]
@@ -513,6 +515,7 @@ struct RecurArgs {
   float* state;         // [32][128 k][128 v]
   float* out;           // [n][4096]
   unsigned n, np, nc, zab_stride;
+  unsigned c_begin, c_end;  // chunks of this launch: the state is read at c_begin, written after
   float eps;
 };
 
@@ -615,7 +618,8 @@ __global__ void __launch_bounds__(kRecurThreads, 1)
   }
   RecurBars& bar = *reinterpret_cast<RecurBars*>(smem + kOffBar);
   const unsigned h = blockIdx.x, warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const unsigned nc = a.nc;
+  // Chunk c of this launch (local index, for buffer parities) is chunk c0 + c of the sequence.
+  const unsigned nc = a.nc, c0 = a.c_begin, ncl = a.c_end - a.c_begin;
   const uint32_t sbase = dev::smem_u32(smem);
   const float* egh = a.eg + size_t(h) * a.np;
 
@@ -655,16 +659,16 @@ __global__ void __launch_bounds__(kRecurThreads, 1)
       dev::tma_prefetch_desc(&qgmap);
       dev::tma_prefetch_desc(&vmap);
       unsigned staged = 0, p1in = 0;  // chunks whose stage / U inputs have been issued
-      for (unsigned c = 0; c < nc; ++c) {
-        const unsigned s = c & 1;
-        const int row = int((h * nc + c) * kC);
+      for (unsigned c = 0; c < ncl; ++c) {
+        const unsigned s = c & 1, cg = c0 + c;
+        const int row = int((h * nc + cg) * kC);
         if (c >= 2 && !wait_or_abort(bar, bar.p1in_empty[s], ((c >> 1) & 1) ^ 1))
           break;
         const uint32_t pb = sbase + kOffP1 + s * kP1Bytes, pfull = dev::smem_u32(&bar.p1in_full[s]);
         dev::mbar_arrive_expect_tx(pfull, kP1Bytes);
         for (int x = 0; x < 2; ++x) {
-          dev::tma_load_3d(pb + kP1Vh + x * kTile, &vmap, x * 64, h, c * kC, pfull);
-          dev::tma_load_3d(pb + kP1Vl + x * kTile, &vlmap, x * 64, h, c * kC, pfull);
+          dev::tma_load_3d(pb + kP1Vh + x * kTile, &vmap, x * 64, h, cg * kC, pfull);
+          dev::tma_load_3d(pb + kP1Vl + x * kTile, &vlmap, x * 64, h, cg * kC, pfull);
         }
         dev::tma_load_2d(pb + kP1Tu, &tumap, 0, row, pfull);
         p1in = c + 1;
@@ -721,7 +725,7 @@ __global__ void __launch_bounds__(kRecurThreads, 1)
         dev::tc_fence_after();
         issue_u(0);
       }
-      for (unsigned c = 0; ok && c < nc; ++c) {
+      for (unsigned c = 0; ok && c < ncl; ++c) {
         const unsigned b = c & 1;
         const uint32_t sb = sbase + b * kStageBytes;
         if (!poll_or_abort(bar, bar.stage_full[b], (c >> 1) & 1) ||
@@ -735,7 +739,7 @@ __global__ void __launch_bounds__(kRecurThreads, 1)
                              kdesc(sb + kStB + (ks >> 2) * 2 * kTile + (ks & 3) * 32), id_xy,
                              ks > 0);
         dev::tc_commit(dev::smem_u32(&bar.x_full));
-        if (c + 1 < nc) {
+        if (c + 1 < ncl) {
           if (!poll_or_abort(bar, bar.p1in_full[(c + 1) & 1], ((c + 1) >> 1) & 1))
             break;
           dev::tc_fence_after();
@@ -771,8 +775,8 @@ __global__ void __launch_bounds__(kRecurThreads, 1)
     const uint32_t trow = tmem + ((32u * q) << 16);
     const float* S = a.state + size_t(h) * kDim * kDim;
     bool ok = true;
-    for (unsigned c = 0; ok && c < nc; ++c) {
-      const float el = egh[c * kC + kC - 1];  // e^(g_last)
+    for (unsigned c = 0; ok && c < ncl; ++c) {
+      const float el = egh[(c0 + c) * kC + kC - 1];  // e^(g_last)
       // E0: fp16 copy of S^T (the A operand of XY), then S^T *= e^(g_last) for the update.
       if (c > 0 && !warp_wait(bar, bar.s_full, (c - 1) & 1)) {
         ok = false;
@@ -839,7 +843,7 @@ __global__ void __launch_bounds__(kRecurThreads, 1)
       warp_arrive(bar.d_ready);
     }
     // Final state back to [k][v] (coalesced over v).
-    if (ok && warp_wait(bar, bar.s_full, (nc - 1) & 1)) {
+    if (ok && warp_wait(bar, bar.s_full, (ncl - 1) & 1)) {
       dev::tc_fence_after();
       float* So = a.state + size_t(h) * kDim * kDim;
 #pragma unroll 1
@@ -867,8 +871,8 @@ __global__ void __launch_bounds__(kRecurThreads, 1)
     const float* zh = a.z + h * kDim + v;
     float* out_v = a.out + h * kDim + v;
     constexpr int kG = 8, kT = 32;
-    for (unsigned c = 0; c < nc; ++c) {
-      const unsigned b = c & 1, t0 = c * kC + kT * oh;
+    for (unsigned c = 0; c < ncl; ++c) {
+      const unsigned b = c & 1, t0 = (c0 + c) * kC + kT * oh;
       const uint32_t ocol = trow + kColO + kT * oh;
       // Tokens past the end read the last token's gate (their outputs are not stored).
       float zr[kT];
