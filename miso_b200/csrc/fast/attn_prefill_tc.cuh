@@ -14,9 +14,9 @@
 //                      tile's columns; the pair exchanges row maxima through shared memory):
 //                      causal mask on diagonal tiles only, online max (rescaling O only when
 //                      the max grows by more than 2^8, then exactly), P = 2^(s - m) as fp16
-//                      into 128B-swizzled shared memory
-//   O += P_j V_j       tcgen05.mma M=128 N=256 K=64 (4 x K16), A = P (K-major), B = V (MN-major)
-// Roles: warps 0 and 2 issue TMA (Q and K; V; both double-buffered), warp 1 owns TMEM and issues every MMA
+//                      written into TMEM over the S tile it came from (two values per column)
+//   O += P_j V_j       tcgen05.mma M=128 N=256 K=64 (4 x K16), A = P from TMEM, B = V (MN-major)
+// Roles: warps 0 and 2 issue TMA (Q and K, 3 K stages; V, 2 stages), warp 1 owns TMEM and issues every MMA
 // from one thread, warps 4-11 run softmax, O correction and the epilogue (O / l * sigmoid(gate),
 // each warp staging its 32 rows through shared memory so global stores and gate loads are
 // row-contiguous). Control decisions inside a softmax warp are warp-uniform (__all_sync), as the
@@ -49,21 +49,21 @@ constexpr uint32_t kQBox = kRows * 64 * 2;      // one 64-dim slab of Q: 16 KB
 constexpr uint32_t kKVBox = kBN * 64 * 2;       // one 64-dim slab of a K / V tile: 8 KB
 constexpr uint32_t kQBytes = 4 * kQBox;         // 64 KB
 constexpr uint32_t kKVBytes = 4 * kKVBox;       // 32 KB
-constexpr uint32_t kPBytes = kRows * kBN * 2;   // 16 KB
+constexpr int kKStages = 3, kVStages = 2;
 constexpr uint32_t kOffQ = 0;
-constexpr uint32_t kOffK = kOffQ + kQBytes;        // 2 stages
-constexpr uint32_t kOffV = kOffK + 2 * kKVBytes;   // 2 stages
-constexpr uint32_t kOffP = kOffV + 2 * kKVBytes;   // 2 buffers
-constexpr uint32_t kOffRed = kOffP + 2 * kPBytes;  // [2 parity][2 column half][128 rows] f32
+constexpr uint32_t kOffK = kOffQ + kQBytes;
+constexpr uint32_t kOffV = kOffK + kKStages * kKVBytes;
+constexpr uint32_t kOffRed = kOffV + kVStages * kKVBytes;  // [2 parity][2 column half][128 rows] f32
 constexpr uint32_t kOffBar = kOffRed + 2 * 2 * kRows * 4;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 0;    // O accumulator: 256 columns
-constexpr uint32_t kColS = 256;  // S buffers: 2 x 64 columns
+constexpr int kSBufs = 2;
+constexpr uint32_t kColS = 256;  // S buffers: kSBufs x 64 columns (P of the tile overwrites 32 of them)
 
 struct Bars {
   uint64_t q_full;
-  uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
-  uint64_t s_full[2], s_free[2], p_full[2], pv_done[2];
+  uint64_t k_full[kKStages], k_empty[kKStages], v_full[kVStages], v_empty[kVStages];
+  uint64_t s_full[kSBufs], p_full[kSBufs], pv_done[2];
   uint64_t xchg[4][2];  // per TMEM lane quadrant and tile parity: the two softmax warps' partials
   uint64_t drain;
   uint32_t tmem_base;
@@ -71,8 +71,9 @@ struct Bars {
 };
 
 constexpr size_t kSmemBytes = kOffBar + sizeof(Bars);  // base must be 1024-byte aligned
-static_assert(kOffK - kOffQ == kQBytes && kOffV - kOffK == 2 * kKVBytes, "layout");
-static_assert(2 * (2 * kKVBytes) == kRows * kDim * 4, "O staging reuses the K and V stages");
+static_assert(kOffK - kOffQ == kQBytes && kOffV - kOffK == kKStages * kKVBytes, "layout");
+static_assert((kKStages + kVStages) * kKVBytes >= kRows * kDim * 4,
+              "O staging reuses the K and V stages");
 
 struct Args {
   const float* qg;
@@ -116,17 +117,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     dev::mbar_init(dev::smem_u32(&bar.q_full), 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kKStages; ++s) {
       dev::mbar_init(dev::smem_u32(&bar.k_full[s]), 1);
       dev::mbar_init(dev::smem_u32(&bar.k_empty[s]), 1);
+    }
+    for (int s = 0; s < 2; ++s) {
       dev::mbar_init(dev::smem_u32(&bar.v_full[s]), 1);
       dev::mbar_init(dev::smem_u32(&bar.v_empty[s]), 1);
-      dev::mbar_init(dev::smem_u32(&bar.s_full[s]), 1);
-      dev::mbar_init(dev::smem_u32(&bar.s_free[s]), 8);
-      dev::mbar_init(dev::smem_u32(&bar.p_full[s]), 8);
       dev::mbar_init(dev::smem_u32(&bar.pv_done[s]), 1);
       for (int qd = 0; qd < 4; ++qd)
         dev::mbar_init(dev::smem_u32(&bar.xchg[qd][s]), 2);
+    }
+    for (int s = 0; s < kSBufs; ++s) {
+      dev::mbar_init(dev::smem_u32(&bar.s_full[s]), 1);
+      dev::mbar_init(dev::smem_u32(&bar.p_full[s]), 8);
     }
     dev::mbar_init(dev::smem_u32(&bar.drain), 1);
     bar.abort_flag = 0;
@@ -144,7 +148,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 || warp == 2) {
     // ------------------------------------------------------------------------------ producers
     // Warp 0 loads Q and the K tiles, warp 2 the V tiles: the two streams refill independently
-    // (K_j as soon as S_(j-2) has released its stage, V_j as soon as PV_(j-2) has) and each
+    // (K_j as soon as S_(j-3) has released its stage, V_j as soon as PV_(j-2) has) and each
     // producer blocks in a suspending wait.
     if (lane == 0) {
       const bool is_k = warp == 0;
@@ -152,6 +156,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint64_t* full = is_k ? bar.k_full : bar.v_full;
       uint64_t* empty = is_k ? bar.k_empty : bar.v_empty;
       const uint32_t dst0 = sbase + (is_k ? kOffK : kOffV);
+      const unsigned nst = is_k ? kKStages : kVStages;
       dev::tma_prefetch_desc(map);
       if (is_k) {
         dev::tma_prefetch_desc(&qmap);
@@ -162,8 +167,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       unsigned issued = 0;
       for (unsigned j = 0; j < nkv; ++j) {
-        const unsigned s = j & 1, ph = (j >> 1) & 1;
-        if (j >= 2 && !wait_or_abort(bar, empty[s], ph ^ 1))
+        const unsigned s = j % nst, ph = (j / nst) & 1;
+        if (j >= nst && !wait_or_abort(bar, empty[s], ph ^ 1))
           break;
         dev::mbar_arrive_expect_tx(dev::smem_u32(&full[s]), kKVBytes);
         for (int box = 0; box < 4; ++box)
@@ -175,8 +180,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Let the copies already issued land before the CTA exits (bounded waits).
         if (is_k)
           dev::mbar_wait(dev::smem_u32(&bar.q_full), 0);
-        for (unsigned j = issued >= 2 ? issued - 2 : 0; j < issued; ++j)
-          dev::mbar_wait(dev::smem_u32(&full[j & 1]), (j >> 1) & 1);
+        for (unsigned j = issued >= nst ? issued - nst : 0; j < issued; ++j)
+          dev::mbar_wait(dev::smem_u32(&full[j % nst]), (j / nst) & 1);
       }
     }
   } else if (warp == 1) {
@@ -187,45 +192,46 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Descriptors of buffer 0 at k-offset 0; offsets are added to the start-address field.
       const uint64_t qdesc0 = dev::sdesc_sw128(sbase + kOffQ, 16, 1024);
       const uint64_t kdesc0 = dev::sdesc_sw128(sbase + kOffK, 16, 1024);
-      const uint64_t pdesc0 = dev::sdesc_sw128(sbase + kOffP, 16, 1024);
       const uint64_t vdesc0 = dev::sdesc_sw128(sbase + kOffV, kKVBox, 1024);
       bool ok = wait_or_abort(bar, bar.q_full, 0);
       dev::tc_fence_after();
-      // Issue state machine: S(j) goes out as soon as K_j has landed and S buffer j & 1 has been
-      // read by softmax(j - 2); PV(i) as soon as P_i and V_i are ready. Both are polled, so a PV
-      // is never held back behind the next K tile's load (the S / PV order in the tensor pipe
-      // does not matter: they write different TMEM columns; the PVs stay in order).
+      // Issue state machine: S(j) goes out as soon as K_j has landed and PV(j - kSBufs) has been
+      // issued (S buffer j % kSBufs holds P_(j - kSBufs) until that PV has read it; the tensor
+      // pipe runs in issue order); PV(i) as soon as P_i and V_i are ready. Both are polled, so a
+      // PV is never held back behind the next K tile's load. (A third S buffer measured the
+      // same: the pipe itself is then the bound, QK^T being N = 64 MMAs.)
       unsigned ns = 0, np = 0;  // next S and next PV to issue
       long long last = clock64();
       while (ok && np < nkv) {
         bool progressed = false;
-        if (ns < nkv) {
-          const unsigned s = ns & 1, ph = (ns >> 1) & 1;
-          if (dev::mbar_test_wait(dev::smem_u32(&bar.k_full[s]), ph) &&
-              (ns < 2 || dev::mbar_test_wait(dev::smem_u32(&bar.s_free[s]), ph ^ 1))) {
+        if (ns < nkv && (ns < kSBufs || np + kSBufs > ns)) {
+          const unsigned s = ns % kSBufs, kst = ns % kKStages, kph = (ns / kKStages) & 1;
+          if (dev::mbar_test_wait(dev::smem_u32(&bar.k_full[kst]), kph)) {
             dev::tc_fence_after();
             const uint32_t d = tmem + kColS + s * kBN;
-            const uint64_t kd = kdesc0 + ((s * kKVBytes) >> 4);
+            const uint64_t kd = kdesc0 + ((kst * kKVBytes) >> 4);
 #pragma unroll
             for (int ks = 0; ks < kDim / 16; ++ks)
               dev::tc_mma_f16_ss(d, qdesc0 + (((ks >> 2) * kQBox + (ks & 3) * 32) >> 4),
                                  kd + (((ks >> 2) * kKVBox + (ks & 3) * 32) >> 4), idesc_s, ks > 0);
             dev::tc_commit(dev::smem_u32(&bar.s_full[s]));
-            dev::tc_commit(dev::smem_u32(&bar.k_empty[s]));
+            dev::tc_commit(dev::smem_u32(&bar.k_empty[kst]));
             ++ns;
             progressed = true;
           }
         }
         if (np < ns) {
           const unsigned i = np, s = i & 1, ph = (i >> 1) & 1;
-          if (dev::mbar_test_wait(dev::smem_u32(&bar.p_full[s]), ph) &&
+          const unsigned sb = i % kSBufs, sph = (i / kSBufs) & 1;
+          if (dev::mbar_test_wait(dev::smem_u32(&bar.p_full[sb]), sph) &&
               dev::mbar_test_wait(dev::smem_u32(&bar.v_full[s]), ph)) {
             dev::tc_fence_after();
-            const uint64_t pd = pdesc0 + ((s * kPBytes) >> 4), vd = vdesc0 + ((s * kKVBytes) >> 4);
+            const uint32_t pa = tmem + kColS + sb * kBN;  // P_i: 64 keys as 32 fp16 pairs
+            const uint64_t vd = vdesc0 + ((s * kKVBytes) >> 4);
 #pragma unroll
             for (int kk = 0; kk < kBN / 16; ++kk)
-              dev::tc_mma_f16_ss(tmem + kColO, pd + ((kk * 32) >> 4), vd + ((kk * 2048) >> 4),
-                                 idesc_o, (i > 0 || kk > 0) ? 1u : 0u);
+              dev::tc_mma_f16_ts(tmem + kColO, pa + 8 * kk, vd + ((kk * 2048) >> 4), idesc_o,
+                                 (i > 0 || kk > 0) ? 1u : 0u);
             dev::tc_commit(dev::smem_u32(&bar.pv_done[s]));
             dev::tc_commit(dev::smem_u32(&bar.v_empty[s]));
             ++np;
@@ -276,7 +282,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       return true;
     };
     for (unsigned j = 0; j < nkv; ++j) {
-      const unsigned s = j & 1, ph = (j >> 1) & 1;
+      const unsigned s = j % kSBufs, ph = (j / kSBufs) & 1;  // S / P buffer of tile j
       if (!__all_sync(0xffffffffu, wait_or_abort(bar, bar.s_full[s], ph))) {
         ok = false;
         break;
@@ -285,10 +291,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t x[32];
       dev::tmem_ld32(trow + kColS + s * kBN + 32 * hc, x);
       dev::tmem_wait_ld();
-      dev::tc_fence_before();
-      __syncwarp();
-      if (lane == 0)
-        dev::mbar_arrive(dev::smem_u32(&bar.s_free[s]));
       // Raw scores (the scale is folded into the exponent's FMA below; it is positive, so the
       // maximum commutes with it).
       const unsigned key0 = j * kBN + 32 * hc;
@@ -339,30 +341,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         l *= corr;
         m_ref = m_new;
       }
-      if (j >= 2 &&  // P buffer s is free once PV_{j-2} has completed
-          !__all_sync(0xffffffffu, wait_or_abort(bar, bar.pv_done[s], ph ^ 1))) {
-        ok = false;
-        break;
-      }
-      uint8_t* prow = base + kOffP + s * kPBytes + r * 128;
+      // P overwrites this warp's half of P's 32 columns in the S buffer: both warps of the pair
+      // have read their S halves before the exchange above, so nothing unread is overwritten.
       const float neg_m = -m_ref;
       float lsum0 = 0.0f, lsum1 = 0.0f;
+      uint32_t pk[16];
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
-        __align__(16) __half2 h[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float p0 = dev::ex2_approx(fmaf(v[8 * c4 + 2 * e], sl2, neg_m));
-          const float p1 = dev::ex2_approx(fmaf(v[8 * c4 + 2 * e + 1], sl2, neg_m));
-          h[e] = __floats2half2_rn(p0, p1);
-          lsum0 += p0;
-          lsum1 += p1;
-        }
-        *reinterpret_cast<uint4*>(prow + (((4 * hc + c4) ^ (r & 7)) << 4)) =
-            *reinterpret_cast<const uint4*>(h);
+      for (int e = 0; e < 16; ++e) {
+        const float p0 = dev::ex2_approx(fmaf(v[2 * e], sl2, neg_m));
+        const float p1 = dev::ex2_approx(fmaf(v[2 * e + 1], sl2, neg_m));
+        const __half2 h2v = __floats2half2_rn(p0, p1);
+        pk[e] = *reinterpret_cast<const uint32_t*>(&h2v);
+        lsum0 += p0;
+        lsum1 += p1;
       }
+      dev::tmem_st16(trow + kColS + s * kBN + 16 * hc, pk);
       l += lsum0 + lsum1;
-      dev::fence_proxy_async_smem();
+      dev::tmem_wait_st();
       dev::tc_fence_before();
       __syncwarp();
       if (lane == 0)
