@@ -730,11 +730,15 @@ def bench_cp_block(args, dev, stream, max_over_ranks, barrier, world, rank) -> d
     # wavefront's idle segments.
     # Higher priority: when attention CTAs retire, the block scheduler starts the wavefront's
     # CTAs first, so the sequential DeltaNet chain is not queued behind the whole attention grid.
-    dn_stream = torch.cuda.Stream(device=dev, priority=-1)
+    dn_stream = torch.cuda.Stream(device=dev, priority=-100)  # clamped to the highest
     dn_group = None
     if world > 1:
         import torch.distributed as dist
-        dn_group = dist.new_group(list(range(world)), backend="nccl")
+        # The state hand-off's NCCL kernels run on the communicator's own stream: at normal
+        # priority the block scheduler holds them behind the attention grid's pending CTAs, so a
+        # rank's DeltaNet could start only once the whole attention layer had been dispatched.
+        opts = dist.ProcessGroupNCCL.Options(is_high_priority_stream=True)
+        dn_group = dist.new_group(list(range(world)), backend="nccl", pg_options=opts)
     attn = cp.GpuAttentionCp(t, world, rank, proj, ones, ones, inv, EPS, stream)
     dn = cp.GpuDeltaNetWavefront(t, world, rank, projs, conv_w, ssm_a, dt, norm_w, EPS,
                                  dn_stream, group=dn_group)
