@@ -456,9 +456,10 @@ int miso_attn_prefill_tc(const miso_attn_prefill_tc_params* p, void* stream) {
   {
     const cuuint64_t dims[3] = {256, uint64_t(p->pos0) + p->n, 2};
     const cuuint64_t strides[2] = {256 * 2, uint64_t(p->max_ctx) * 256 * 2};
-    const cuuint32_t box[3] = {64, 64, 1};
-    if ((st = f16_map(&kmap, p->k_cache, 3, dims, strides, box)) != MISO_OK ||
-        (st = f16_map(&vmap, p->v_cache, 3, dims, strides, box)) != MISO_OK)
+    const cuuint32_t kbox[3] = {64, pf::kBN, 1};  // 64 dims x one tile's keys
+    const cuuint32_t vbox[3] = {64, 64, 1};       // 64 dims x 64 keys
+    if ((st = f16_map(&kmap, p->k_cache, 3, dims, strides, kbox)) != MISO_OK ||
+        (st = f16_map(&vmap, p->v_cache, 3, dims, strides, vbox)) != MISO_OK)
       return st;
   }
   pf::Args a;

@@ -8,15 +8,20 @@
 // share it. Tiles are launched longest first (the causal triangle makes late tokens the most
 // work), so the block scheduler approximates a longest-processing-time order.
 //
-// Per KV tile j of 64 keys:
-//   S_j = Q K_j^T      tcgen05.mma M=128 N=64 K=256 (16 x K16), fp16 x fp16 -> fp32 in TMEM
+// Per KV tile j of 128 keys:
+//   S_j = Q K_j^T      tcgen05.mma M=128 N=128 K=256 (16 x K16; K arrives as two 128-dim halves),
+//                      fp16 x fp16 -> fp32 in TMEM
 //   softmax            8 warps, two per TMEM lane quadrant (one thread per row and half of the
 //                      tile's columns; the pair exchanges row maxima through shared memory):
 //                      causal mask on diagonal tiles only, online max (rescaling O only when
 //                      the max grows by more than 2^8, then exactly), P = 2^(s - m) as fp16
 //                      written into TMEM over the S tile it came from (two values per column)
-//   O += P_j V_j       tcgen05.mma M=128 N=256 K=64 (4 x K16), A = P from TMEM, B = V (MN-major)
-// Roles: warps 0 and 2 issue TMA (Q and K, 3 K stages; V, 2 stages), warp 1 owns TMEM and issues every MMA
+//   O += P_j V_j       tcgen05.mma M=128 N=256 K=128 (8 x K16, V as two 64-key halves), A = P from
+//                      TMEM, B = V (MN-major)
+// With head dimension 256 a whole 128-key K or V tile (64 KB) does not fit twice next to Q, so K
+// streams through a ring of 128-dim halves and V through a ring of 64-key halves (32 KB each);
+// N = 128 for Q K^T runs at 97% of the tensor rate against 65% for N = 64.
+// Roles: warps 0 and 2 issue TMA (Q and K halves, 3 slots; V halves, 2 slots), warp 1 owns TMEM and issues every MMA
 // from one thread, warps 4-11 run softmax, O correction and the epilogue (O / l * sigmoid(gate),
 // each warp staging its 32 rows through shared memory so global stores and gate loads are
 // row-contiguous). Control decisions inside a softmax warp are warp-uniform (__all_sync), as the
@@ -43,22 +48,23 @@ namespace miso::fast::prefill {
 constexpr int kQHeads = 16, kKvHeads = 2, kDim = 256, kGroup = 8;
 constexpr int kTokens = 16;  // tokens per query tile; x 8 heads = 128 rows
 constexpr int kRows = 128;
-constexpr int kBN = 64;  // keys per KV tile
+constexpr int kBN = 128;  // keys per KV tile
 constexpr int kThreads = 384;  // warps 0 / 2 TMA, warp 1 MMA + TMEM, warps 4-11 softmax
 constexpr uint32_t kQBox = kRows * 64 * 2;      // one 64-dim slab of Q: 16 KB
-constexpr uint32_t kKVBox = kBN * 64 * 2;       // one 64-dim slab of a K / V tile: 8 KB
+constexpr uint32_t kKBox = kBN * 64 * 2;        // one 64-dim slab of 128 keys: 16 KB
+constexpr uint32_t kVBox = 64 * 64 * 2;         // one 64-dim slab of 64 keys: 8 KB
 constexpr uint32_t kQBytes = 4 * kQBox;         // 64 KB
-constexpr uint32_t kKVBytes = 4 * kKVBox;       // 32 KB
-constexpr int kKStages = 3, kVStages = 2;
+constexpr uint32_t kHalfBytes = 32768;          // a K half (2 slabs) or a V half (4 slabs)
+constexpr int kKStages = 3, kVStages = 2;       // ring slots of K halves / V halves
 constexpr uint32_t kOffQ = 0;
 constexpr uint32_t kOffK = kOffQ + kQBytes;
-constexpr uint32_t kOffV = kOffK + kKStages * kKVBytes;
-constexpr uint32_t kOffRed = kOffV + kVStages * kKVBytes;  // [2 parity][2 column half][128 rows] f32
+constexpr uint32_t kOffV = kOffK + kKStages * kHalfBytes;
+constexpr uint32_t kOffRed = kOffV + kVStages * kHalfBytes;  // [2 parity][2 column half][128 rows] f32
 constexpr uint32_t kOffBar = kOffRed + 2 * 2 * kRows * 4;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 0;    // O accumulator: 256 columns
 constexpr int kSBufs = 2;
-constexpr uint32_t kColS = 256;  // S buffers: kSBufs x 64 columns (P of the tile overwrites 32 of them)
+constexpr uint32_t kColS = 256;  // S buffers: kSBufs x 128 columns (P of the tile overwrites 64 of them)
 
 struct Bars {
   uint64_t q_full;
@@ -71,9 +77,11 @@ struct Bars {
 };
 
 constexpr size_t kSmemBytes = kOffBar + sizeof(Bars);  // base must be 1024-byte aligned
-static_assert(kOffK - kOffQ == kQBytes && kOffV - kOffK == kKStages * kKVBytes, "layout");
-static_assert((kKStages + kVStages) * kKVBytes >= kRows * kDim * 4,
+static_assert(2 * kKBox == kHalfBytes && 4 * kVBox == kHalfBytes, "ring slot size");
+static_assert(kColS + kSBufs * kBN <= kTmemCols, "TMEM columns");
+static_assert((kKStages + kVStages) * kHalfBytes >= kRows * kDim * 4,
               "O staging reuses the K and V stages");
+static_assert(kSmemBytes <= 232448, "fits the 227 KB opt-in shared memory");
 
 struct Args {
   const float* qg;
@@ -147,9 +155,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0 || warp == 2) {
     // ------------------------------------------------------------------------------ producers
-    // Warp 0 loads Q and the K tiles, warp 2 the V tiles: the two streams refill independently
-    // (K_j as soon as S_(j-3) has released its stage, V_j as soon as PV_(j-2) has) and each
-    // producer blocks in a suspending wait.
+    // Warp 0 loads Q and the K halves, warp 2 the V halves: the two rings refill independently
+    // (half u of a ring as soon as the MMAs reading half u - slots have completed) and each
+    // producer blocks in a suspending wait. Half u of K is dims [128 (u % 2), +128) of the 128
+    // keys of tile u / 2; half u of V is keys [64 u, 64 u + 64) with all 256 dims.
     if (lane == 0) {
       const bool is_k = warp == 0;
       const CUtensorMap* map = is_k ? &kmap : &vmap;
@@ -166,22 +175,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                            dev::smem_u32(&bar.q_full));
       }
       unsigned issued = 0;
-      for (unsigned j = 0; j < nkv; ++j) {
-        const unsigned s = j % nst, ph = (j / nst) & 1;
-        if (j >= nst && !wait_or_abort(bar, empty[s], ph ^ 1))
+      for (unsigned u = 0; u < 2 * nkv; ++u) {
+        const unsigned s = u % nst, ph = (u / nst) & 1;
+        if (u >= nst && !wait_or_abort(bar, empty[s], ph ^ 1))
           break;
-        dev::mbar_arrive_expect_tx(dev::smem_u32(&full[s]), kKVBytes);
-        for (int box = 0; box < 4; ++box)
-          dev::tma_load_3d(dst0 + s * kKVBytes + box * kKVBox, map, box * 64, j * kBN, kvh,
-                           dev::smem_u32(&full[s]));
-        issued = j + 1;
+        const uint32_t fb = dev::smem_u32(&full[s]), dst = dst0 + s * kHalfBytes;
+        dev::mbar_arrive_expect_tx(fb, kHalfBytes);
+        if (is_k) {
+          for (int box = 0; box < 2; ++box)
+            dev::tma_load_3d(dst + box * kKBox, map, 128 * (u & 1) + 64 * box, (u >> 1) * kBN, kvh,
+                             fb);
+        } else {
+          for (int box = 0; box < 4; ++box)
+            dev::tma_load_3d(dst + box * kVBox, map, 64 * box, 64 * u, kvh, fb);
+        }
+        issued = u + 1;
       }
       if (aborted(bar)) {
         // Let the copies already issued land before the CTA exits (bounded waits).
         if (is_k)
           dev::mbar_wait(dev::smem_u32(&bar.q_full), 0);
-        for (unsigned j = issued >= nst ? issued - nst : 0; j < issued; ++j)
-          dev::mbar_wait(dev::smem_u32(&full[j % nst]), (j / nst) & 1);
+        for (unsigned u = issued >= nst ? issued - nst : 0; u < issued; ++u)
+          dev::mbar_wait(dev::smem_u32(&full[u % nst]), (u / nst) & 1);
       }
     }
   } else if (warp == 1) {
@@ -189,51 +204,59 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       const uint32_t idesc_s = dev::idesc_f16_f32(kRows, kBN, 0, 0);
       const uint32_t idesc_o = dev::idesc_f16_f32(kRows, kDim, 0, 1);
-      // Descriptors of buffer 0 at k-offset 0; offsets are added to the start-address field.
+      // Descriptors at offset 0; offsets are added to the start-address field.
       const uint64_t qdesc0 = dev::sdesc_sw128(sbase + kOffQ, 16, 1024);
       const uint64_t kdesc0 = dev::sdesc_sw128(sbase + kOffK, 16, 1024);
-      const uint64_t vdesc0 = dev::sdesc_sw128(sbase + kOffV, kKVBox, 1024);
+      const uint64_t vdesc0 = dev::sdesc_sw128(sbase + kOffV, kVBox, 1024);
       bool ok = wait_or_abort(bar, bar.q_full, 0);
       dev::tc_fence_after();
-      // Issue state machine: S(j) goes out as soon as K_j has landed and PV(j - kSBufs) has been
-      // issued (S buffer j % kSBufs holds P_(j - kSBufs) until that PV has read it; the tensor
-      // pipe runs in issue order); PV(i) as soon as P_i and V_i are ready. Both are polled, so a
-      // PV is never held back behind the next K tile's load. (A third S buffer measured the
-      // same: the pipe itself is then the bound, QK^T being N = 64 MMAs.)
+      // Issue state machine: S(j) goes out as soon as both K halves of tile j have landed and
+      // PV(j - kSBufs) has been issued (S buffer j % kSBufs holds P_(j - kSBufs) until that PV has
+      // read it; the tensor pipe runs in issue order); PV(i) as soon as P_i and both V halves of
+      // tile i are ready. Both are polled, so a PV is never held back behind the next K load.
       unsigned ns = 0, np = 0;  // next S and next PV to issue
       long long last = clock64();
       while (ok && np < nkv) {
         bool progressed = false;
         if (ns < nkv && (ns < kSBufs || np + kSBufs > ns)) {
-          const unsigned s = ns % kSBufs, kst = ns % kKStages, kph = (ns / kKStages) & 1;
-          if (dev::mbar_test_wait(dev::smem_u32(&bar.k_full[kst]), kph)) {
+          const unsigned u0 = 2 * ns, s0 = u0 % kKStages, s1 = (u0 + 1) % kKStages;
+          if (dev::mbar_test_wait(dev::smem_u32(&bar.k_full[s0]), (u0 / kKStages) & 1) &&
+              dev::mbar_test_wait(dev::smem_u32(&bar.k_full[s1]), ((u0 + 1) / kKStages) & 1)) {
             dev::tc_fence_after();
-            const uint32_t d = tmem + kColS + s * kBN;
-            const uint64_t kd = kdesc0 + ((kst * kKVBytes) >> 4);
+            const uint32_t d = tmem + kColS + (ns % kSBufs) * kBN;
 #pragma unroll
-            for (int ks = 0; ks < kDim / 16; ++ks)
-              dev::tc_mma_f16_ss(d, qdesc0 + (((ks >> 2) * kQBox + (ks & 3) * 32) >> 4),
-                                 kd + (((ks >> 2) * kKVBox + (ks & 3) * 32) >> 4), idesc_s, ks > 0);
-            dev::tc_commit(dev::smem_u32(&bar.s_full[s]));
-            dev::tc_commit(dev::smem_u32(&bar.k_empty[kst]));
+            for (int h = 0; h < 2; ++h) {
+              const uint64_t kd = kdesc0 + (((h ? s1 : s0) * kHalfBytes) >> 4);
+#pragma unroll
+              for (int ks = 0; ks < 8; ++ks)
+                dev::tc_mma_f16_ss(
+                    d, qdesc0 + ((((2 * h + (ks >> 2)) * kQBox) + (ks & 3) * 32) >> 4),
+                    kd + (((ks >> 2) * kKBox + (ks & 3) * 32) >> 4), idesc_s, (h | ks) != 0);
+              dev::tc_commit(dev::smem_u32(&bar.k_empty[h ? s1 : s0]));
+            }
+            dev::tc_commit(dev::smem_u32(&bar.s_full[ns % kSBufs]));
             ++ns;
             progressed = true;
           }
         }
         if (np < ns) {
-          const unsigned i = np, s = i & 1, ph = (i >> 1) & 1;
-          const unsigned sb = i % kSBufs, sph = (i / kSBufs) & 1;
+          const unsigned i = np, sb = i % kSBufs, sph = (i / kSBufs) & 1;
+          // V halves 2i and 2i + 1 sit in slots 0 and 1 (two slots), phase i & 1.
           if (dev::mbar_test_wait(dev::smem_u32(&bar.p_full[sb]), sph) &&
-              dev::mbar_test_wait(dev::smem_u32(&bar.v_full[s]), ph)) {
+              dev::mbar_test_wait(dev::smem_u32(&bar.v_full[0]), i & 1) &&
+              dev::mbar_test_wait(dev::smem_u32(&bar.v_full[1]), i & 1)) {
             dev::tc_fence_after();
-            const uint32_t pa = tmem + kColS + sb * kBN;  // P_i: 64 keys as 32 fp16 pairs
-            const uint64_t vd = vdesc0 + ((s * kKVBytes) >> 4);
+            const uint32_t pa = tmem + kColS + sb * kBN;  // P_i: 128 keys as 64 fp16 pairs
 #pragma unroll
-            for (int kk = 0; kk < kBN / 16; ++kk)
-              dev::tc_mma_f16_ts(tmem + kColO, pa + 8 * kk, vd + ((kk * 2048) >> 4), idesc_o,
-                                 (i > 0 || kk > 0) ? 1u : 0u);
-            dev::tc_commit(dev::smem_u32(&bar.pv_done[s]));
-            dev::tc_commit(dev::smem_u32(&bar.v_empty[s]));
+            for (int h = 0; h < 2; ++h) {
+              const uint64_t vd = vdesc0 + ((h * kHalfBytes) >> 4);
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk)
+                dev::tc_mma_f16_ts(tmem + kColO, pa + 32 * h + 8 * kk, vd + ((kk * 2048) >> 4),
+                                   idesc_o, (i > 0 || h > 0 || kk > 0) ? 1u : 0u);
+              dev::tc_commit(dev::smem_u32(&bar.v_empty[h]));
+            }
+            dev::tc_commit(dev::smem_u32(&bar.pv_done[i & 1]));
             ++np;
             progressed = true;
           }
@@ -257,7 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp >= 4) {
     // --------------------------------------------------------------- softmax and epilogue
     // Two warps per TMEM lane quadrant: warp (4 + q + 4 hc) holds rows [32 q, 32 q + 32) and
-    // S columns [32 hc, 32 hc + 32) of each tile, O columns [128 hc, 128 hc + 128).
+    // S columns [64 hc, 64 hc + 64) of each tile, O columns [128 hc, 128 hc + 128).
     const unsigned q = warp & 3, hc = (warp - 4) >> 2;
     const unsigned r = 32 * q + lane;
     const uint32_t trow = tmem + ((32u * q) << 16);
@@ -288,27 +311,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       dev::tc_fence_after();
-      uint32_t x[32];
-      dev::tmem_ld32(trow + kColS + s * kBN + 32 * hc, x);
+      float v[64];
+      dev::tmem_ld32(trow + kColS + s * kBN + 64 * hc, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+      dev::tmem_ld32(trow + kColS + s * kBN + 64 * hc + 32,
+                     *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
       dev::tmem_wait_ld();
       // Raw scores (the scale is folded into the exponent's FMA below; it is positive, so the
-      // maximum commutes with it).
-      const unsigned key0 = j * kBN + 32 * hc;
-      float v[32];
-      float mx = kNegInf;
-      if (key0 + 31 <= pos_min) {  // interior tile half: no masking
+      // maximum commutes with it). Four partial maxima keep the dependency chain short.
+      const unsigned key0 = j * kBN + 64 * hc;
+      float mx4[4] = {kNegInf, kNegInf, kNegInf, kNegInf};
+      if (key0 + 63 <= pos_min) {  // interior tile half: no masking
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          v[c] = __uint_as_float(x[c]);
-          mx = fmaxf(mx, v[c]);
-        }
+        for (int c = 0; c < 64; ++c)
+          mx4[c & 3] = fmaxf(mx4[c & 3], v[c]);
       } else {
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          v[c] = key0 + c <= pos ? __uint_as_float(x[c]) : kNegInf;
-          mx = fmaxf(mx, v[c]);
+        for (int c = 0; c < 64; ++c) {
+          v[c] = key0 + c <= pos ? v[c] : kNegInf;
+          mx4[c & 3] = fmaxf(mx4[c & 3], v[c]);
         }
       }
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       float mx_other;
       if (!exchange(j, mx, mx_other)) {
         ok = false;
@@ -341,22 +364,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         l *= corr;
         m_ref = m_new;
       }
-      // P overwrites this warp's half of P's 32 columns in the S buffer: both warps of the pair
+      // P overwrites this warp's half of P's 64 columns in the S buffer: both warps of the pair
       // have read their S halves before the exchange above, so nothing unread is overwritten.
       const float neg_m = -m_ref;
-      float lsum0 = 0.0f, lsum1 = 0.0f;
-      uint32_t pk[16];
+      float lsum[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      uint32_t pk[32];
 #pragma unroll
-      for (int e = 0; e < 16; ++e) {
+      for (int e = 0; e < 32; ++e) {
         const float p0 = dev::ex2_approx(fmaf(v[2 * e], sl2, neg_m));
         const float p1 = dev::ex2_approx(fmaf(v[2 * e + 1], sl2, neg_m));
         const __half2 h2v = __floats2half2_rn(p0, p1);
         pk[e] = *reinterpret_cast<const uint32_t*>(&h2v);
-        lsum0 += p0;
-        lsum1 += p1;
+        lsum[e & 3] += p0 + p1;
       }
-      dev::tmem_st16(trow + kColS + s * kBN + 16 * hc, pk);
-      l += lsum0 + lsum1;
+      dev::tmem_st32(trow + kColS + s * kBN + 32 * hc, pk);
+      l += (lsum[0] + lsum[1]) + (lsum[2] + lsum[3]);
       dev::tmem_wait_st();
       dev::tc_fence_before();
       __syncwarp();
