@@ -373,7 +373,7 @@ PREFILL_N = 8192
 DECODE_TRAFFIC_PER_ALGORITHMIC_BYTE = (257.0 + 6.3) / 256.8
 # ncu DRAM bytes (read + write) of one full-size launch (profiles/prefill_kernel_8k_ncu.md,
 # profiles/deltanet_prefill_tc_8k_ncu.md).
-PREFILL_8K_TRAFFIC = (220.8 + 101.0) * 1e6
+PREFILL_8K_TRAFFIC = (221.3 + 101.5) * 1e6
 DN_PREFILL_8K_TRAFFIC = (270.8 + 229.1 + 136.5 + 247.3 + 573.4 + 119.4) * 1e6
 
 
