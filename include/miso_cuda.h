@@ -334,6 +334,18 @@ size_t miso_deltanet_prefill_tc_scratch_bytes(unsigned n);
 int miso_deltanet_prefill_tc(const miso_deltanet_seq_params* p, void* scratch, size_t scratch_bytes,
                              void* stream);
 
+/* The same prefill in two calls, for callers that run the part that does not depend on the state
+ * ahead of the state's arrival (a context-parallel wavefront receives the state of a segment from
+ * the rank before it). _front: the conv, the per-chunk tiles and the conv history; reads qkv, a,
+ * b, conv_w, conv_in, ssm_a, dt_bias, writes conv_out and the scratch, and neither reads nor
+ * writes the state. _recur: the recurrence; reads the scratch written by a _front call with the
+ * same p->n and the same scratch, and z, norm_w and the state; writes the state (in place) and
+ * out. _front followed by _recur equals miso_deltanet_prefill_tc bit for bit. */
+int miso_deltanet_prefill_tc_front(const miso_deltanet_seq_params* p, void* scratch,
+                                   size_t scratch_bytes, void* stream);
+int miso_deltanet_prefill_tc_recur(const miso_deltanet_seq_params* p, void* scratch,
+                                   size_t scratch_bytes, void* stream);
+
 /* ---------------------------------------------------------------------------------------------
  * Library state
  * ------------------------------------------------------------------------------------------- */

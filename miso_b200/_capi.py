@@ -111,6 +111,10 @@ SIGNATURES = {
     "miso_deltanet_step_batched": (C.c_int, [C.POINTER(DeltaNetStepBatchedParams), _P]),
     "miso_deltanet_prefill_tc_scratch_bytes": (C.c_size_t, [_U]),
     "miso_deltanet_prefill_tc": (C.c_int, [C.POINTER(DeltaNetSeqParams), _P, C.c_size_t, _P]),
+    "miso_deltanet_prefill_tc_front": (C.c_int, [C.POINTER(DeltaNetSeqParams), _P, C.c_size_t,
+                                                 _P]),
+    "miso_deltanet_prefill_tc_recur": (C.c_int, [C.POINTER(DeltaNetSeqParams), _P, C.c_size_t,
+                                                 _P]),
     "miso_attn_prep_batch_f16": (C.c_int, [C.POINTER(AttnPrepBatchParams), _P, _P]),
     "miso_device_status": (C.c_int, [C.c_int, C.POINTER(C.c_int)]),
     "miso_version": (C.c_char_p, []),

@@ -9,9 +9,12 @@ tensor-core prefill of its two query chunks against all keys before them
 (miso_attn_prefill_tc with pos0 = chunk start).
 
 Gated DeltaNet layers: the recurrence needs the state at the end of the previous tokens, so the
-sequence is cut into W contiguous segments and the state (with the conv history) is handed from
-rank r - 1 to rank r. Independent layers form a wavefront: rank r runs layer l while rank r + 1
-runs layer l - 1, so L layers take (W + L - 1) segment times instead of W L.
+sequence is cut into W contiguous segments and the state is handed from rank r - 1 to rank r.
+Only the recurrence waits for it: the causal conv of a segment needs just the last three input
+rows before it (a halo exchanged up front), and the per-chunk tiles depend on the inputs only, so
+every rank runs that front part of all its layers at once, and the hand-off chain carries the
+recurrences alone. Independent layers form a wavefront: rank r runs layer l's recurrence while
+rank r + 1 runs layer l - 1's, so L layers take (W + L - 1) recurrence times.
 
 The orchestration is written against small callables (compute a segment, send / receive a state,
 all-gather a chunk) so that the same code runs over NCCL with the CUDA kernels and over gloo with
@@ -78,31 +81,51 @@ class AttentionCp:
 @dataclass
 class DeltaNetWavefront:
     """One rank's share of L independent Gated DeltaNet layers over a sequence cut into W
-    contiguous segments.
+    contiguous segments (each at least three tokens long).
 
-    run(layer, start, n)   prefill of tokens [start, start + n) of `layer` on the local state
-    reset(layer)           zero state and conv history (rank 0, the start of the sequence)
-    recv(layer)            receive layer's state and conv history from rank - 1
-    send(layer)            send them to rank + 1
+    reset(layer)             zero state and conv history (rank 0, the start of the sequence)
+    halo_recv(layer)         receive this segment's conv history (the three input rows before it)
+                             from rank - 1
+    halo_send(layer)         send the last three input rows of this segment to rank + 1
+    front(layer, start, n)   the part of the segment's prefill that does not need the state
+    recur(layer, start, n)   the recurrence over tokens [start, start + n) from the local state
+    recv(layer)              receive layer's state from rank - 1
+    send(layer)              send it to rank + 1
     """
     t: int
     world: int
     rank: int
     layers: int
-    run_segment: Callable[[int, int, int], None]
+    front: Callable[[int, int, int], None]
+    recur: Callable[[int, int, int], None]
     reset: Callable[[int], None]
+    halo_recv: Callable[[int], None]
+    halo_send: Callable[[int], None]
     recv: Callable[[int], None]
     send: Callable[[int], None]
 
     def run(self) -> None:
         start, n = contiguous_segment(self.t, self.world, self.rank)
+        if n < 3:
+            raise ValueError(f"DeltaNet segments need at least 3 tokens (t={self.t}, "
+                             f"world={self.world})")
+        last = self.rank + 1 == self.world
+        # Raw-input halos first: no compute behind them, so the chain of small messages clears
+        # while the fronts run.
         for layer in range(self.layers):
             if self.rank == 0:
                 self.reset(layer)
             else:
+                self.halo_recv(layer)
+            if not last:
+                self.halo_send(layer)
+        for layer in range(self.layers):
+            self.front(layer, start, n)
+        for layer in range(self.layers):
+            if self.rank > 0:
                 self.recv(layer)
-            self.run_segment(layer, start, n)
-            if self.rank + 1 < self.world:
+            self.recur(layer, start, n)
+            if not last:
                 self.send(layer)
 
 
@@ -175,10 +198,12 @@ class GpuAttentionCp:
 
 class GpuDeltaNetWavefront:
     """Buffers and kernels of one rank's share of L independent DeltaNet layers over projection
-    buffers projs[l] [t][12352]: the rank runs miso_deltanet_prefill_tc on its contiguous segment
-    with the state and conv history received from rank - 1 and passes them on to rank + 1.
-    After run(), self.state[l] / self.conv[l] hold the layer's state after the rank's segment
-    (the final state of the sequence on the last rank) and self.out[l] [t][4096] its rows."""
+    buffers projs[l] [t][12352]: the rank runs miso_deltanet_prefill_tc_front on its contiguous
+    segment of every layer as soon as the conv halo (the three input rows before the segment)
+    has arrived, then, per layer, miso_deltanet_prefill_tc_recur from the state received from
+    rank - 1, and passes the state on to rank + 1. After run(), self.state[l] / self.conv[l] hold
+    the layer's state and conv history after the rank's segment (those of the whole sequence on
+    the last rank) and self.out[l] [t][4096] its rows."""
 
     def __init__(self, t: int, world: int, rank: int, projs, conv_w, ssm_a, dt_bias, norm_w,
                  eps: float, stream, group=None):
@@ -194,41 +219,62 @@ class GpuDeltaNetWavefront:
         self.conv = [torch.zeros((8192, 3), device=dev) for _ in range(L)]
         self.conv_out = [torch.zeros((8192, 3), device=dev) for _ in range(L)]
         self.out = [torch.empty((t, 4096), device=dev) for _ in range(L)]
-        _, n = contiguous_segment(t, world, rank)
+        self.start, n = contiguous_segment(t, world, rank)
         self.sb = self.lib.miso_deltanet_prefill_tc_scratch_bytes(n)
-        self.scratch = torch.empty(self.sb, dtype=torch.uint8, device=dev)
-        self.wf = DeltaNetWavefront(t, world, rank, L, self._run, self._reset, self._recv,
-                                    self._send)
+        # One scratch per layer: every layer's front runs before the first recurrence.
+        self.scratch = [torch.empty(self.sb, dtype=torch.uint8, device=dev) for _ in range(L)]
+        self.wf = DeltaNetWavefront(t, world, rank, L, self._front, self._recur, self._reset,
+                                    self._halo_recv, self._halo_send, self._recv, self._send)
 
-    def _run(self, layer: int, start: int, n: int) -> None:
-        import ctypes
+    def _params(self, layer: int, start: int, n: int):
         capi = self.capi
         conv_w, ssm_a, dt, norm_w = self.w
         base = self.projs[layer].data_ptr() + start * DN_PROJ * 4
         z = base + 8192 * 4
-        p = capi.DeltaNetSeqParams(base, z, z + 4096 * 4, z + 4128 * 4, conv_w.data_ptr(),
-                                   self.conv[layer].data_ptr(), self.conv_out[layer].data_ptr(),
-                                   ssm_a.data_ptr(), dt.data_ptr(), norm_w.data_ptr(),
-                                   self.state[layer].data_ptr(),
-                                   self.out[layer].data_ptr() + start * 4096 * 4, n, self.eps,
-                                   DN_PROJ, DN_PROJ)
-        capi.check("miso_deltanet_prefill_tc", self.lib.miso_deltanet_prefill_tc(
-            ctypes.byref(p), self.scratch.data_ptr(), self.sb, self.stream.cuda_stream))
+        return capi.DeltaNetSeqParams(base, z, z + 4096 * 4, z + 4128 * 4, conv_w.data_ptr(),
+                                      self.conv[layer].data_ptr(),
+                                      self.conv_out[layer].data_ptr(), ssm_a.data_ptr(),
+                                      dt.data_ptr(), norm_w.data_ptr(),
+                                      self.state[layer].data_ptr(),
+                                      self.out[layer].data_ptr() + start * 4096 * 4, n, self.eps,
+                                      DN_PROJ, DN_PROJ)
+
+    def _front(self, layer: int, start: int, n: int) -> None:
+        import ctypes
+        p = self._params(layer, start, n)
+        self.capi.check("miso_deltanet_prefill_tc_front", self.lib.miso_deltanet_prefill_tc_front(
+            ctypes.byref(p), self.scratch[layer].data_ptr(), self.sb, self.stream.cuda_stream))
         self.conv[layer], self.conv_out[layer] = self.conv_out[layer], self.conv[layer]
+
+    def _recur(self, layer: int, start: int, n: int) -> None:
+        import ctypes
+        p = self._params(layer, start, n)
+        self.capi.check("miso_deltanet_prefill_tc_recur", self.lib.miso_deltanet_prefill_tc_recur(
+            ctypes.byref(p), self.scratch[layer].data_ptr(), self.sb, self.stream.cuda_stream))
 
     def _reset(self, layer: int) -> None:
         self.state[layer].zero_()
         self.conv[layer].zero_()
 
+    def _halo_recv(self, layer: int) -> None:
+        import torch.distributed as dist
+        dist.recv(self.conv[layer], self.rank - 1, group=self.group)
+
+    def _halo_send(self, layer: int) -> None:
+        import torch.distributed as dist
+        _, n = contiguous_segment(self.t, self.world, self.rank)
+        end = self.start + n
+        # conv history layout [channel][slot], slot 0 the oldest of the three rows
+        halo = self.projs[layer][end - 3:end, :8192].t().contiguous()
+        dist.send(halo, self.rank + 1, group=self.group)
+
     def _recv(self, layer: int) -> None:
         import torch.distributed as dist
         dist.recv(self.state[layer], self.rank - 1, group=self.group)
-        dist.recv(self.conv[layer], self.rank - 1, group=self.group)
 
     def _send(self, layer: int) -> None:
         import torch.distributed as dist
         dist.send(self.state[layer], self.rank + 1, group=self.group)
-        dist.send(self.conv[layer], self.rank + 1, group=self.group)
 
     def run(self) -> None:
         import torch

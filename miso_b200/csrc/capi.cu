@@ -539,8 +539,14 @@ size_t miso_deltanet_prefill_tc_scratch_bytes(unsigned n) {
   return n == 0 ? 0 : dn_chunk_scratch(n).total;
 }
 
-int miso_deltanet_prefill_tc(const miso_deltanet_seq_params* p, void* scratch, size_t scratch_bytes,
-                             void* stream) {
+}  // extern "C"
+
+namespace {
+
+// Stages of the tensor-core DeltaNet prefill: bit 0 = conv + prepare (no state access), bit 1 =
+// the recurrence (reads the scratch bit 0 wrote).
+int dn_prefill_tc(const miso_deltanet_seq_params* p, void* scratch, size_t scratch_bytes,
+                  void* stream, int stages) {
   namespace dc = miso::fast::dnchunk;
   if (p == nullptr || p->qkv == nullptr || p->z == nullptr || p->a == nullptr ||
       p->b == nullptr || p->conv_w == nullptr || p->conv_in == nullptr ||
@@ -669,21 +675,45 @@ int miso_deltanet_prefill_tc(const miso_deltanet_seq_params* p, void* scratch, s
   // recurrence of earlier ones on a second stream was measured slower: the recurrence is
   // latency-bound and slows down next to other kernels, and every extra launch of it refills
   // its pipeline.)
-  ca.t_begin = 0;
-  dc::conv_kernel<<<dim3(8, (p->n + dc::kConvTokens - 1) / dc::kConvTokens), dc::kConvThreads, 0,
-                    s>>>(ca);
-  if ((st = launch_status()) != MISO_OK)
-    return st;
-  pa.c_begin = 0;
-  dc::prepare_kernel<<<dim3(nc, 16), dc::kPrepThreads, dc::kPrepSmemBytes, s>>>(qmap, kmap, qlmap,
-                                                                                 klmap, pa);
-  if ((st = launch_status()) != MISO_OK)
-    return st;
-  ra.c_begin = 0;
-  ra.c_end = nc;
-  dc::recur_kernel<<<32, dc::kRecurThreads, dc::kRecurSmemBytes, s>>>(
-      wmap, qgmap, ksmap, vmap, vlmap, tumap, aqkmap, aqklmap, ra);
-  return launch_status();
+  if (stages & 1) {
+    ca.t_begin = 0;
+    dc::conv_kernel<<<dim3(8, (p->n + dc::kConvTokens - 1) / dc::kConvTokens), dc::kConvThreads,
+                      0, s>>>(ca);
+    if ((st = launch_status()) != MISO_OK)
+      return st;
+    pa.c_begin = 0;
+    dc::prepare_kernel<<<dim3(nc, 16), dc::kPrepThreads, dc::kPrepSmemBytes, s>>>(
+        qmap, kmap, qlmap, klmap, pa);
+    if ((st = launch_status()) != MISO_OK)
+      return st;
+  }
+  if (stages & 2) {
+    ra.c_begin = 0;
+    ra.c_end = nc;
+    dc::recur_kernel<<<32, dc::kRecurThreads, dc::kRecurSmemBytes, s>>>(
+        wmap, qgmap, ksmap, vmap, vlmap, tumap, aqkmap, aqklmap, ra);
+    return launch_status();
+  }
+  return MISO_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int miso_deltanet_prefill_tc(const miso_deltanet_seq_params* p, void* scratch, size_t scratch_bytes,
+                             void* stream) {
+  return dn_prefill_tc(p, scratch, scratch_bytes, stream, 3);
+}
+
+int miso_deltanet_prefill_tc_front(const miso_deltanet_seq_params* p, void* scratch,
+                                   size_t scratch_bytes, void* stream) {
+  return dn_prefill_tc(p, scratch, scratch_bytes, stream, 1);
+}
+
+int miso_deltanet_prefill_tc_recur(const miso_deltanet_seq_params* p, void* scratch,
+                                   size_t scratch_bytes, void* stream) {
+  return dn_prefill_tc(p, scratch, scratch_bytes, stream, 2);
 }
 
 }  // extern "C"

@@ -74,7 +74,10 @@ def deltanet_case(rank: int, world: int) -> None:
     conv = [np.zeros((8192, 3)) for _ in range(layers)]
     out = [np.zeros((t, 4096)) for _ in range(layers)]
 
-    def run_segment(layer, start, n):
+    def front(layer, start, n):
+        pass  # the oracle runs the conv and the recurrence together in recur()
+
+    def recur(layer, start, n):
         x = ins[layer]
         out[layer][start:start + n] = oracle.deltanet_seq(
             n, x["qkv"][start:start + n], 8192, x["zab"][start:start + n], 4160, x["conv_w"],
@@ -84,17 +87,26 @@ def deltanet_case(rank: int, world: int) -> None:
         state[layer][:] = 0
         conv[layer][:] = 0
 
+    def halo_recv(layer):
+        buf = torch.empty(conv[layer].shape, dtype=torch.float64)
+        dist.recv(buf, rank - 1)
+        conv[layer][:] = buf.numpy()
+
+    def halo_send(layer):
+        start, n = cp.contiguous_segment(t, world, rank)
+        rows = ins[layer]["qkv"][start + n - 3:start + n].astype(np.float64)  # [3][8192]
+        dist.send(torch.from_numpy(np.ascontiguousarray(rows.T)), rank + 1)
+
     def recv(layer):
-        for a in (state[layer], conv[layer]):
-            buf = torch.empty(a.shape, dtype=torch.float64)
-            dist.recv(buf, rank - 1)
-            a[:] = buf.numpy()
+        buf = torch.empty(state[layer].shape, dtype=torch.float64)
+        dist.recv(buf, rank - 1)
+        state[layer][:] = buf.numpy()
 
     def send(layer):
-        for a in (state[layer], conv[layer]):
-            dist.send(torch.from_numpy(a.copy()), rank + 1)
+        dist.send(torch.from_numpy(state[layer].copy()), rank + 1)
 
-    cp.DeltaNetWavefront(t, world, rank, layers, run_segment, reset, recv, send).run()
+    cp.DeltaNetWavefront(t, world, rank, layers, front, recur, reset, halo_recv, halo_send, recv,
+                         send).run()
     for layer in range(layers):
         total = torch.from_numpy(out[layer])
         dist.all_reduce(total)

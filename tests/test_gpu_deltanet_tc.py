@@ -20,7 +20,9 @@ pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda")
 
 
-def run_tc(x, state=None, conv_in=None):
+def run_tc(x, state=None, conv_in=None, split=False):
+    """One miso_deltanet_prefill_tc call, or (split=True) the _front / _recur pair with a scratch
+    buffer whose previous contents are garbage and a state that the front must not touch."""
     n = x["n"]
     lib = capi.load()
     d = {k: T(x[k]) for k in ("qkv", "zab", "conv_w", "ssm_a", "dt", "norm_w")}
@@ -35,8 +37,18 @@ def run_tc(x, state=None, conv_in=None):
     p = capi.DeltaNetSeqParams(ptr(d["qkv"]), zb, zb + 4096 * 4, zb + 4128 * 4, ptr(d["conv_w"]),
                                ptr(ci), ptr(co), ptr(d["ssm_a"]), ptr(d["dt"]), ptr(d["norm_w"]),
                                ptr(st), ptr(out), n, 1e-6, zs, x["qkv"].shape[1])
-    capi.check("miso_deltanet_prefill_tc",
-               lib.miso_deltanet_prefill_tc(C.byref(p), ptr(scratch), sb, None))
+    if split:
+        scratch.fill_(0xA5)
+        st_before = st.clone()
+        capi.check("miso_deltanet_prefill_tc_front",
+                   lib.miso_deltanet_prefill_tc_front(C.byref(p), ptr(scratch), sb, None))
+        torch.cuda.synchronize()
+        assert torch.equal(st, st_before), "the front stage wrote the state"
+        capi.check("miso_deltanet_prefill_tc_recur",
+                   lib.miso_deltanet_prefill_tc_recur(C.byref(p), ptr(scratch), sb, None))
+    else:
+        capi.check("miso_deltanet_prefill_tc",
+                   lib.miso_deltanet_prefill_tc(C.byref(p), ptr(scratch), sb, None))
     torch.cuda.synchronize()
     return out.cpu().numpy(), st.cpu().numpy(), co.cpu().numpy()
 
@@ -119,6 +131,19 @@ def test_prefill_tc_chained_calls_hand_off_state_and_history():
     assert rel(np.concatenate([o1, o2]), ref) <= 1e-3
     assert rel(s2, s64) <= 1e-3
     assert np.array_equal(c2.astype(np.float64), conv64)
+
+
+@pytest.mark.parametrize("n", [5, 64, 300, 2048])
+def test_front_then_recur_equals_one_call_bitwise(n):
+    """The two-stage form used by the context-parallel wavefront (conv + tiles first, the
+    recurrence once the state is there) gives the one-call results bit for bit."""
+    x = config4a_inputs(n, seed=3)
+    x["state"] = (0.1 * np.random.RandomState(4).standard_normal((32, 128, 128))).astype(np.float32)
+    x["conv_in"] = np.random.RandomState(5).standard_normal((8192, 3)).astype(np.float32)
+    o1, s1, c1 = run_tc(x)
+    o2, s2, c2 = run_tc(x, split=True)
+    assert np.array_equal(o1, o2) and np.array_equal(s1, s2) and np.array_equal(c1, c2)
+    assert status_clear()
 
 
 @pytest.mark.parametrize("n", [8192])
