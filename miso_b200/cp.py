@@ -221,8 +221,13 @@ class GpuDeltaNetWavefront:
         self.out = [torch.empty((t, 4096), device=dev) for _ in range(L)]
         self.start, n = contiguous_segment(t, world, rank)
         self.sb = self.lib.miso_deltanet_prefill_tc_scratch_bytes(n)
-        # One scratch per layer: every layer's front runs before the first recurrence.
+        # One scratch per layer: every layer's front is issued before the first recurrence.
         self.scratch = [torch.empty(self.sb, dtype=torch.uint8, device=dev) for _ in range(L)]
+        # The fronts run on their own stream (highest priority; PyTorch clamps the value), so the
+        # front of layer l + 1 overlaps the recurrence of layer l instead of queueing before it.
+        self.front_stream = torch.cuda.Stream(device=dev, priority=-100)
+        self.halo_done = torch.cuda.Event()
+        self.front_done = [torch.cuda.Event() for _ in range(L)]
         self.wf = DeltaNetWavefront(t, world, rank, L, self._front, self._recur, self._reset,
                                     self._halo_recv, self._halo_send, self._recv, self._send)
 
@@ -241,13 +246,19 @@ class GpuDeltaNetWavefront:
 
     def _front(self, layer: int, start: int, n: int) -> None:
         import ctypes
+        if layer == 0:  # the halos (received on self.stream) precede every front
+            self.halo_done.record(self.stream)
+            self.front_stream.wait_event(self.halo_done)
         p = self._params(layer, start, n)
         self.capi.check("miso_deltanet_prefill_tc_front", self.lib.miso_deltanet_prefill_tc_front(
-            ctypes.byref(p), self.scratch[layer].data_ptr(), self.sb, self.stream.cuda_stream))
+            ctypes.byref(p), self.scratch[layer].data_ptr(), self.sb,
+            self.front_stream.cuda_stream))
+        self.front_done[layer].record(self.front_stream)
         self.conv[layer], self.conv_out[layer] = self.conv_out[layer], self.conv[layer]
 
     def _recur(self, layer: int, start: int, n: int) -> None:
         import ctypes
+        self.stream.wait_event(self.front_done[layer])
         p = self._params(layer, start, n)
         self.capi.check("miso_deltanet_prefill_tc_recur", self.lib.miso_deltanet_prefill_tc_recur(
             ctypes.byref(p), self.scratch[layer].data_ptr(), self.sb, self.stream.cuda_stream))
