@@ -426,8 +426,9 @@ int miso_attn_prep_batch_f16(const miso_attn_prep_batch_params* p, uint16_t* q_f
   a.n = p->n;
   a.proj_stride = p->proj_stride;
   a.eps = p->tok0.eps;
-  miso::fast::prep::prefill_prep_kernel<<<p->n, miso::fast::prep::kThreads, 0,
-                                          as_stream(stream)>>>(a);
+  miso::fast::prep::prefill_prep_kernel<<<(p->n + miso::fast::prep::kPrepTokens - 1) /
+                                              miso::fast::prep::kPrepTokens,
+                                          miso::fast::prep::kThreads, 0, as_stream(stream)>>>(a);
   return launch_status();
 }
 

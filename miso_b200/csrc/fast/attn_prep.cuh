@@ -59,7 +59,11 @@ __global__ void __launch_bounds__(kThreads) prep_batched_kernel(Args a) {
 
 // Prefill prep for the tensor-core prefill: attn_prep_batch_kernel (kernels/attention_prefill.hpp)
 // with the queries stored as fp16 [n][16][256] (the operand type of the tcgen05 prefill). One block
-// per token, one warp per head; same arithmetic as the drop-in prep up to the final rounding.
+// per kPrepTokens tokens, one warp per head; each warp issues the loads of all its tokens before
+// the first row's arithmetic. The rotation angles depend only on the position, so warp i < 4
+// computes token i's 32 (sin, cos) pairs once (one per lane) for all 18 heads: the drop-in prep
+// spends most of its instructions on 8 serial sincosf in 8 lanes of every row. Same arithmetic as
+// the drop-in prep (attn_detail::prep_row_math) up to the final rounding.
 struct PrefillArgs {
   const float* qg;
   const float* k;
@@ -74,23 +78,50 @@ struct PrefillArgs {
   float eps;
 };
 
+constexpr unsigned kPrepTokens = 4;
+
 __global__ void __launch_bounds__(kThreads) prefill_prep_kernel(PrefillArgs a) {
   using namespace miso::kernels;
   using namespace miso::kernels::attn;
-  const unsigned t = blockIdx.x, head = threadIdx.x / 32;
-  if (t >= a.n)
+  const unsigned t0 = blockIdx.x * kPrepTokens, head = threadIdx.x / 32;
+  if (t0 >= a.n)
     return;
-  const unsigned pos = a.pos0 + t;
-  const size_t row = size_t(t) * a.proj_stride;
-  if (head < kQHeads) {
-    attn_detail::prep_row_warp(a.qg + row + head * 2 * kDim, a.q_norm, a.inv_freq, pos, a.eps,
-                               nullptr, a.q16 + (size_t(t) * kQHeads + head) * kDim, nullptr,
-                               nullptr);
-  } else {
-    const unsigned kvh = head - kQHeads;
-    const size_t at = (size_t(kvh) * a.max_ctx + pos) * kDim;
-    attn_detail::prep_row_warp(a.k + row + kvh * kDim, a.k_norm, a.inv_freq, pos, a.eps, nullptr,
-                               a.k_cache + at, a.v + row + kvh * kDim, a.v_cache + at);
+  const unsigned nt = min(kPrepTokens, a.n - t0);
+  const bool is_q = head < kQHeads;
+  const unsigned kvh = head - kQHeads;
+  const float* src0 = is_q ? a.qg + head * 2 * kDim : a.k + kvh * kDim;
+  __shared__ float2 sc[kPrepTokens][kRopeDim / 2];
+  if (head < kPrepTokens && head < nt) {
+    const unsigned lane = threadIdx.x % 32;
+    float sn, cs;
+    sincosf(static_cast<float>(a.pos0 + t0 + head) * a.inv_freq[lane], &sn, &cs);
+    sc[head][lane] = make_float2(sn, cs);
+  }
+  float y[kPrepTokens][8], v[kPrepTokens][8], w[8];
+  attn_detail::load_row8(is_q ? a.q_norm : a.k_norm, w);
+#pragma unroll
+  for (unsigned i = 0; i < kPrepTokens; ++i) {
+    if (i < nt) {
+      const size_t row = size_t(t0 + i) * a.proj_stride;
+      attn_detail::load_row8(src0 + row, y[i]);
+      if (!is_q)
+        attn_detail::load_row8(a.v + row + kvh * kDim, v[i]);
+    }
+  }
+  __syncthreads();  // the (sin, cos) tables
+#pragma unroll
+  for (unsigned i = 0; i < kPrepTokens; ++i) {
+    if (i < nt) {
+      const unsigned pos = a.pos0 + t0 + i;
+      attn_detail::prep_row_math_table(y[i], w, sc[i], a.eps);
+      if (is_q) {
+        attn_detail::store_row8_f16(y[i], a.q16 + (size_t(t0 + i) * kQHeads + head) * kDim);
+      } else {
+        const size_t at = (size_t(kvh) * a.max_ctx + pos) * kDim;
+        attn_detail::store_row8_f16(y[i], a.k_cache + at);
+        attn_detail::store_row8_f16(v[i], a.v_cache + at);
+      }
+    }
   }
 }
 

@@ -51,25 +51,13 @@ struct AttnPrepBatchParams {
 
 namespace attn_detail {
 
-// One row of 256 (a query head or a key head) on one warp, lane l owning dims [8l, 8l + 8):
-// RMSNorm with `weight`, NEOX rotation of dims [0, 64) at position `pos` (dim d < 32 pairs with
-// d + 32, i.e. lane l < 4 with lane l + 4), then either an fp32 store (out_f32) or an fp16 store
-// (out_f16, plus the matching value row v_src -> v_dst when v_src is given). Warp-synchronous, no
-// shared memory, so the drop-in and batched prep kernels produce identical bits.
-__device__ __forceinline__ void prep_row_warp(const float* src, const float* weight,
-                                              const float* inv_freq, unsigned pos, float eps,
-                                              float* out_f32, attn::half_t* out_f16,
-                                              const float* v_src, attn::half_t* v_dst) {
+// RMSNorm with `w` and the NEOX rotation of dims [0, 64) at position `pos` of one row of 256 held
+// by a warp, lane l owning dims [8l, 8l + 8) in y (dim d < 32 pairs with d + 32, i.e. lane l < 4
+// with lane l + 4). Warp-synchronous.
+__device__ __forceinline__ void prep_row_math(float (&y)[8], const float (&w)[8],
+                                              const float* inv_freq, unsigned pos, float eps) {
   using namespace attn;
   const unsigned lane = threadIdx.x % kWave;
-  float y[8], w[8];
-  const float4* s4 = reinterpret_cast<const float4*>(src) + 2 * lane;
-  const float4* w4 = reinterpret_cast<const float4*>(weight) + 2 * lane;
-  {
-    const float4 a = s4[0], b = s4[1], c = w4[0], d = w4[1];
-    y[0] = a.x, y[1] = a.y, y[2] = a.z, y[3] = a.w, y[4] = b.x, y[5] = b.y, y[6] = b.z, y[7] = b.w;
-    w[0] = c.x, w[1] = c.y, w[2] = c.z, w[3] = c.w, w[4] = d.x, w[5] = d.y, w[6] = d.z, w[7] = d.w;
-  }
   float ss = 0.0f;
 #pragma unroll
   for (int i = 0; i < 8; ++i)
@@ -92,25 +80,77 @@ __device__ __forceinline__ void prep_row_warp(const float* src, const float* wei
       y[i] = d < kHalf ? y[i] * cs - partner[i] * sn : y[i] * cs + partner[i] * sn;
     }
   }
+}
+
+// prep_row_math with the rotation's (sin, cos) taken from a table: sc[f] = sincos(pos *
+// inv_freq[f]) for the 32 frequencies f of the position (the same values prep_row_math computes,
+// so the results are identical; the table is shared by all heads of a token).
+__device__ __forceinline__ void prep_row_math_table(float (&y)[8], const float (&w)[8],
+                                                    const float2* sc, float eps) {
+  using namespace attn;
+  const unsigned lane = threadIdx.x % kWave;
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    ss += y[i] * y[i];
+  const float inv_rms = rsqrtf(wave_sum(ss) / kDim + eps);
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    y[i] = y[i] * inv_rms * w[i];
+  float partner[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    partner[i] = __shfl_xor_sync(0xffffffffu, y[i], 4);
+  if (lane < kRopeDim / 8) {
+    constexpr unsigned kHalf = kRopeDim / 2;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const unsigned d = 8 * lane + i;
+      const float2 t = sc[d % kHalf];
+      y[i] = d < kHalf ? y[i] * t.y - partner[i] * t.x : y[i] * t.y + partner[i] * t.x;
+    }
+  }
+}
+
+// Lane's 8 consecutive floats of a row of 256.
+__device__ __forceinline__ void load_row8(const float* row, float (&y)[8]) {
+  const float4* r4 = reinterpret_cast<const float4*>(row) + 2 * (threadIdx.x % kWave);
+  const float4 a = r4[0], b = r4[1];
+  y[0] = a.x, y[1] = a.y, y[2] = a.z, y[3] = a.w, y[4] = b.x, y[5] = b.y, y[6] = b.z, y[7] = b.w;
+}
+
+// Lane's 8 values of a row of 256 as fp16 (one 16-byte store).
+__device__ __forceinline__ void store_row8_f16(const float (&y)[8], attn::half_t* row) {
+  __align__(16) __half h[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    h[i] = __float2half_rn(y[i]);
+  reinterpret_cast<uint4*>(row)[threadIdx.x % kWave] = *reinterpret_cast<const uint4*>(h);
+}
+
+// One row of 256 (a query head or a key head) on one warp: prep_row_math, then either an fp32
+// store (out_f32) or an fp16 store (out_f16, plus the matching value row v_src -> v_dst when
+// v_src is given). Warp-synchronous, no shared memory, so the drop-in and batched prep kernels
+// produce identical bits.
+__device__ __forceinline__ void prep_row_warp(const float* src, const float* weight,
+                                              const float* inv_freq, unsigned pos, float eps,
+                                              float* out_f32, attn::half_t* out_f16,
+                                              const float* v_src, attn::half_t* v_dst) {
+  float y[8], w[8];
+  load_row8(src, y);
+  load_row8(weight, w);
+  prep_row_math(y, w, inv_freq, pos, eps);
   if (out_f32 != nullptr) {
-    float4* o4 = reinterpret_cast<float4*>(out_f32) + 2 * lane;
+    float4* o4 = reinterpret_cast<float4*>(out_f32) + 2 * (threadIdx.x % kWave);
     o4[0] = make_float4(y[0], y[1], y[2], y[3]);
     o4[1] = make_float4(y[4], y[5], y[6], y[7]);
   } else {
-    __align__(16) __half h[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-      h[i] = __float2half_rn(y[i]);
-    reinterpret_cast<uint4*>(out_f16)[lane] = *reinterpret_cast<const uint4*>(h);
+    store_row8_f16(y, out_f16);
     if (v_src == nullptr)
       return;
-    const float4* v4 = reinterpret_cast<const float4*>(v_src) + 2 * lane;
-    const float4 a = v4[0], b = v4[1];
-    __align__(16) __half hv[8] = {__float2half_rn(a.x), __float2half_rn(a.y),
-                                  __float2half_rn(a.z), __float2half_rn(a.w),
-                                  __float2half_rn(b.x), __float2half_rn(b.y),
-                                  __float2half_rn(b.z), __float2half_rn(b.w)};
-    reinterpret_cast<uint4*>(v_dst)[lane] = *reinterpret_cast<const uint4*>(hv);
+    float v[8];
+    load_row8(v_src, v);
+    store_row8_f16(v, v_dst);
   }
 }
 
