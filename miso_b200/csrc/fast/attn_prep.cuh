@@ -3,7 +3,7 @@
 // Batched decode prep: the per-head RMSNorm + partial NEOX RoPE + KV append of attn_prep_kernel
 // (kernels/attention_decode.hpp) for a batch of sequences, each at its own position. One block
 // per sequence, one warp per head (18 warps), so the block alone owns lens[b] and advances it
-// after the append without a race.
+// after the append without a race (every warp has read lens[b] at the block barrier).
 
 #include <cuda_runtime.h>
 
@@ -35,24 +35,39 @@ constexpr int kThreads = 18 * 32;  // one warp per head: 16 query heads, 2 KV he
 __global__ void __launch_bounds__(kThreads) prep_batched_kernel(Args a) {
   using namespace miso::kernels;
   using namespace miso::kernels::attn;
-  const unsigned b = blockIdx.x, head = threadIdx.x / 32;
+  const unsigned b = blockIdx.x, head = threadIdx.x / 32, lane = threadIdx.x % 32;
   if (b >= a.batch)
     return;
   const unsigned pos = static_cast<unsigned>(a.lens[b]);
   const float* qg = a.qg + size_t(b) * a.proj_stride;
   const float* kk = a.k + size_t(b) * a.proj_stride;
   const float* vv = a.v + size_t(b) * a.proj_stride;
-  if (head < kQHeads) {
-    attn_detail::prep_row_warp(qg + head * 2 * kDim, a.q_norm, a.inv_freq, pos, a.eps,
-                               a.q + (size_t(b) * kQHeads + head) * kDim, nullptr, nullptr,
-                               nullptr);
-  } else {
-    const unsigned kvh = head - kQHeads;
-    const size_t row = size_t(a.kv_row[2 * b + kvh] + pos) * kDim;
-    attn_detail::prep_row_warp(kk + kvh * kDim, a.k_norm, a.inv_freq, pos, a.eps, nullptr,
-                               a.k_pool + row, vv + kvh * kDim, a.v_pool + row);
+  const bool is_q = head < kQHeads;
+  const unsigned kvh = head - kQHeads;
+  float y[8], w[8];
+  attn_detail::load_row8(is_q ? qg + head * 2 * kDim : kk + kvh * kDim, y);
+  attn_detail::load_row8(is_q ? a.q_norm : a.k_norm, w);
+  // The rotation's (sin, cos) depend only on the position: computed once (one per lane) for all
+  // 18 heads, with the same sincosf arguments as attn_detail::prep_row_math.
+  __shared__ float2 sc[kRopeDim / 2];
+  if (head == 0) {
+    float sn, cs;
+    sincosf(static_cast<float>(pos) * a.inv_freq[lane], &sn, &cs);
+    sc[lane] = make_float2(sn, cs);
   }
-  __syncthreads();  // every warp has read lens[b]
+  __syncthreads();  // the table; also: every warp has read lens[b]
+  attn_detail::prep_row_math_table(y, w, sc, a.eps);
+  if (is_q) {
+    float4* o4 = reinterpret_cast<float4*>(a.q + (size_t(b) * kQHeads + head) * kDim) + 2 * lane;
+    o4[0] = make_float4(y[0], y[1], y[2], y[3]);
+    o4[1] = make_float4(y[4], y[5], y[6], y[7]);
+  } else {
+    const size_t row = size_t(a.kv_row[2 * b + kvh] + pos) * kDim;
+    attn_detail::store_row8_f16(y, a.k_pool + row);
+    float v[8];
+    attn_detail::load_row8(vv + kvh * kDim, v);
+    attn_detail::store_row8_f16(v, a.v_pool + row);
+  }
   if (threadIdx.x == 0)
     a.lens[b] = static_cast<int32_t>(pos + 1);
 }
