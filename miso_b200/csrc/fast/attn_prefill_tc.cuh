@@ -21,11 +21,11 @@
 // With head dimension 256 a whole 128-key K or V tile (64 KB) does not fit twice next to Q, so K
 // streams through a ring of 128-dim halves and V through a ring of 64-key halves (32 KB each);
 // N = 128 for Q K^T runs at 97% of the tensor rate against 65% for N = 64.
-// Roles: warps 0 and 2 issue TMA (Q and K halves, 3 slots; V halves, 2 slots), warp 1 owns TMEM and issues every MMA
-// from one thread, warps 4-11 run softmax, O correction and the epilogue (O / l * sigmoid(gate),
-// each warp staging its 32 rows through shared memory so global stores and gate loads are
-// row-contiguous). Control decisions inside a softmax warp are warp-uniform (__all_sync), as the
-// TMEM accesses are warp-collective.
+// Roles: warps 0 and 2 issue TMA (Q and K halves, 3 slots; V halves, 2 slots), warp 1 owns TMEM
+// and issues every MMA from one thread, warps 4-11 run softmax, O correction and the epilogue
+// (O / l * sigmoid(gate), each warp staging its 32 rows through shared memory so global stores
+// and gate loads are row-contiguous). Control decisions inside a softmax warp are warp-uniform
+// (__all_sync), as the TMEM accesses are warp-collective.
 //
 // Precision: K / V are the fp16 cache, Q is fp16, P fp16 (bf16 P would cost ~1.6e-3 relative
 // error), all accumulation fp32. Keys past pos0 + n are outside the K / V tensor maps and
@@ -59,12 +59,14 @@ constexpr int kKStages = 3, kVStages = 2;       // ring slots of K halves / V ha
 constexpr uint32_t kOffQ = 0;
 constexpr uint32_t kOffK = kOffQ + kQBytes;
 constexpr uint32_t kOffV = kOffK + kKStages * kHalfBytes;
-constexpr uint32_t kOffRed = kOffV + kVStages * kHalfBytes;  // [2 parity][2 column half][128 rows] f32
+// Row-max exchange buffer: [2 parity][2 column half][128 rows] fp32.
+constexpr uint32_t kOffRed = kOffV + kVStages * kHalfBytes;
 constexpr uint32_t kOffBar = kOffRed + 2 * 2 * kRows * 4;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 0;    // O accumulator: 256 columns
 constexpr int kSBufs = 2;
-constexpr uint32_t kColS = 256;  // S buffers: kSBufs x 128 columns (P of the tile overwrites 64 of them)
+// S buffers: kSBufs x 128 columns (P of the tile overwrites 64 of them).
+constexpr uint32_t kColS = 256;
 
 struct Bars {
   uint64_t q_full;

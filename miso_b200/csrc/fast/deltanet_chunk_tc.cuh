@@ -800,7 +800,8 @@ __global__ void __launch_bounds__(kRecurThreads, 1)
         uint32_t p16[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e)
-          p16[e] = h2(__uint_as_float(x[32 * part + 2 * e]), __uint_as_float(x[32 * part + 2 * e + 1]));
+          p16[e] = h2(__uint_as_float(x[32 * part + 2 * e]),
+                      __uint_as_float(x[32 * part + 2 * e + 1]));
         dev::tmem_st16(trow + kColS16 + 32 * hc + 16 * part, p16);
       }
       dev::tmem_wait_st();
