@@ -70,3 +70,40 @@ def test_attention_context_parallel_gloo(world):
 @pytest.mark.parametrize("world", [2, 3])
 def test_deltanet_wavefront_gloo(world):
     run_ranks("deltanet", world)
+
+
+@pytest.mark.parametrize("world", [1, 2, 4])
+def test_deltanet_wavefront_call_order(world):
+    """Per rank: the conv halos first (no compute behind them), then the state-independent front
+    of every layer, then per layer receive state -> recurrence -> send state; rank 0 starts from
+    reset() instead of a received halo / state, the last rank sends nothing."""
+    layers, t = 3, 64 * world
+    for rank in range(world):
+        calls = []
+        rec = lambda name: (lambda *a: calls.append((name,) + a))  # noqa: E731
+        wf = cp.DeltaNetWavefront(t, world, rank, layers, rec("front"), rec("recur"),
+                                  rec("reset"), rec("halo_recv"), rec("halo_send"), rec("recv"),
+                                  rec("send"))
+        wf.run()
+        start, n = cp.contiguous_segment(t, world, rank)
+        first, last = rank == 0, rank == world - 1
+        expect = []
+        for layer in range(layers):
+            expect.append(("reset", layer) if first else ("halo_recv", layer))
+            if not last:
+                expect.append(("halo_send", layer))
+        expect += [("front", layer, start, n) for layer in range(layers)]
+        for layer in range(layers):
+            if not first:
+                expect.append(("recv", layer))
+            expect.append(("recur", layer, start, n))
+            if not last:
+                expect.append(("send", layer))
+        assert calls == expect
+
+
+def test_deltanet_wavefront_rejects_segments_shorter_than_the_conv_halo():
+    noop = lambda *a: None  # noqa: E731
+    wf = cp.DeltaNetWavefront(4, 2, 0, 1, noop, noop, noop, noop, noop, noop, noop)
+    with pytest.raises(ValueError):
+        wf.run()
