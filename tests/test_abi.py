@@ -114,8 +114,13 @@ def test_invalid_arguments_are_rejected_without_a_device():
     dp = capi.DeltaNetSeqParams(fake, fake, fake, fake, fake, fake, fake, fake, fake, fake, fake,
                                 fake, 64, 1e-6, 4160, 8192)
     assert lib.miso_deltanet_prefill_tc(C.byref(dp), fake, 1 << 30, None) == -1
+    for stage in (lib.miso_deltanet_prefill_tc_front, lib.miso_deltanet_prefill_tc_recur):
+        assert stage(None, fake, 1 << 30, None) == -1
+        assert stage(C.byref(dp), fake, 1 << 30, None) == -1
     dp.conv_out = fake * 2
     assert lib.miso_deltanet_prefill_tc(C.byref(dp), fake, 1024, None) == -2
+    for stage in (lib.miso_deltanet_prefill_tc_front, lib.miso_deltanet_prefill_tc_recur):
+        assert stage(C.byref(dp), fake, 1024, None) == -2  # the same scratch contract
     st = C.c_int(0)
     assert lib.miso_device_status(0, None) == -1
     assert st.value == 0
