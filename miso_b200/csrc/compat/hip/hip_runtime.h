@@ -7,6 +7,15 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
+// The reference spells binary16 `_Float16`. nvcc 12.9's device front end stops with "unsupported
+// float variant" on C++20 library code instantiated for _Float16 even where only host code uses it
+// (std::vector<_Float16>::resize), so after this header the name means CUDA's __half: the same
+// 2-byte IEEE binary16 layout, with round-to-nearest-even conversions from and to float on the
+// host and the device. (<algorithm> is included because HIP's runtime header provides it.)
+#define _Float16 __half
+
 typedef cudaStream_t hipStream_t;
 typedef cudaError_t hipError_t;
 typedef cudaEvent_t hipEvent_t;
@@ -21,6 +30,10 @@ typedef cudaMemcpyKind hipMemcpyKind;
 #define hipMemcpyHostToHost cudaMemcpyHostToHost
 #define hipMemcpyDefault cudaMemcpyDefault
 #define hipHostMallocDefault cudaHostAllocDefault
+#define hipStreamDefault cudaStreamDefault
+#define hipStreamNonBlocking cudaStreamNonBlocking
+#define hipEventDefault cudaEventDefault
+#define hipEventDisableTiming cudaEventDisableTiming
 
 #define hipMalloc cudaMalloc
 #define hipFree cudaFree
@@ -28,15 +41,16 @@ typedef cudaMemcpyKind hipMemcpyKind;
 #define hipMemcpyAsync cudaMemcpyAsync
 #define hipMemset cudaMemset
 #define hipMemsetAsync cudaMemsetAsync
-#define hipHostMalloc(ptr, size, flags) cudaHostAlloc((ptr), (size), (flags))
 #define hipHostFree cudaFreeHost
 #define hipGetLastError cudaGetLastError
 #define hipPeekAtLastError cudaPeekAtLastError
 #define hipDeviceSynchronize cudaDeviceSynchronize
 #define hipStreamCreate cudaStreamCreate
+#define hipStreamCreateWithFlags cudaStreamCreateWithFlags
 #define hipStreamDestroy cudaStreamDestroy
 #define hipStreamSynchronize cudaStreamSynchronize
 #define hipEventCreate cudaEventCreate
+#define hipEventCreateWithFlags cudaEventCreateWithFlags
 #define hipEventDestroy cudaEventDestroy
 #define hipEventRecord cudaEventRecord
 #define hipEventSynchronize cudaEventSynchronize
@@ -47,6 +61,16 @@ typedef cudaMemcpyKind hipMemcpyKind;
 #define hipGetDeviceProperties cudaGetDeviceProperties
 #define hipSetDevice cudaSetDevice
 #define hipGetDevice cudaGetDevice
+
+// Pinned host allocation; HIP's flags argument defaults to 0 and its default / portable / mapped
+// bits have the CUDA values.
+inline cudaError_t hipHostMalloc(void** ptr, size_t size, unsigned int flags = 0) {
+  return cudaHostAlloc(ptr, size, flags);
+}
+template <class T>
+inline cudaError_t hipHostMalloc(T** ptr, size_t size, unsigned int flags = 0) {
+  return cudaHostAlloc(reinterpret_cast<void**>(ptr), size, flags);
+}
 
 // HIP's width-taking shuffles over the full warp.
 #if defined(__CUDACC__)
