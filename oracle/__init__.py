@@ -22,9 +22,31 @@ LIB = os.path.join(HERE, "libmiso_oracle.so")
 _lib = None
 
 
+REF = os.environ.get("MISO_REFERENCE_DIR",
+                     os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference"))
+REF_QUANT = os.path.join(HERE, "_ref", "libref_quant.so")
+
+
 def build() -> str:
+    """Builds the C oracle; where the reference's sources are present, also its weight-format code
+    (oracle/_ref/libref_quant.so) that pins oracle/quant.py."""
     subprocess.run(["make", "-s", "-C", HERE], check=True)
+    if os.path.exists(os.path.join(REF, "src", "repack.cpp")):
+        subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={REF}"], check=True)
     return LIB
+
+
+def ref_quant():
+    """The reference's dequant / repack code (ctypes), or None when it was not built."""
+    if not os.path.exists(REF_QUANT):
+        return None
+    lib = C.CDLL(REF_QUANT)
+    lib.ref_dequant.argtypes = [C.c_int, C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t]
+    lib.ref_repack_q4k.argtypes = [C.c_void_p, C.c_size_t, C.c_void_p]
+    lib.ref_repack_q6k.argtypes = [C.c_void_p, C.c_size_t, C.c_size_t, C.c_void_p, C.c_size_t]
+    lib.ref_q6k_r1_row_bytes.argtypes = [C.c_size_t]
+    lib.ref_q6k_r1_row_bytes.restype = C.c_size_t
+    return lib
 
 
 def _load() -> C.CDLL:
