@@ -191,29 +191,41 @@ __device__ __forceinline__ float2 q4k_sub_scale(const uint4& h, unsigned j) {
                      gemv::f16_bits(h.x >> 16) * gemv::small_int_f((f >> 6) & 63u));
 }
 
-// sum over l < 32 of q[l] x[a][l] for the 32 elements of sub-block j of a Q4_K r1 block (nibble
-// bytes `qs`: element l is byte 32 (j / 2) + l, low nibble for even j), for every assignment a
-// (x rows of stride `ld` floats, 16-byte aligned).
-template <unsigned kT>
-__device__ __forceinline__ void q4k_sub_dot(const std::uint8_t* qs, unsigned j, const float* x,
-                                            unsigned ld, float (&out)[kT]) {
-  const uint4 q0 = __ldg(reinterpret_cast<const uint4*>(qs + 32 * (j / 2)));
-  const uint4 q1 = __ldg(reinterpret_cast<const uint4*>(qs + 32 * (j / 2) + 16));
+// sum over l < 32 of q[l] x[a][l] for the 32 elements of sub-block j of kM Q4_K r1 blocks (nibble
+// bytes qs[m]: element l is byte 32 (j / 2) + l, low nibble for even j), for every assignment a
+// (x rows of stride `ld` floats, 16-byte aligned). One pass over the activations serves all kM
+// weight rows.
+template <unsigned kT, int kM>
+__device__ __forceinline__ void q4k_sub_dot(const std::uint8_t* const (&qs)[kM], unsigned j,
+                                            const float* x, unsigned ld, float (&out)[kM][kT]) {
+  uint4 q[kM][2];
+#pragma unroll
+  for (int m = 0; m < kM; ++m) {
+    q[m][0] = __ldg(reinterpret_cast<const uint4*>(qs[m] + 32 * (j / 2)));
+    q[m][1] = __ldg(reinterpret_cast<const uint4*>(qs[m] + 32 * (j / 2) + 16));
+  }
   const unsigned sh = 4 * (j % 2);
 #pragma unroll
-  for (unsigned a = 0; a < kT; ++a)
-    out[a] = 0.0f;
+  for (int m = 0; m < kM; ++m)
+#pragma unroll
+    for (unsigned a = 0; a < kT; ++a)
+      out[m][a] = 0.0f;
 #pragma unroll
   for (int v = 0; v < 8; ++v) {
-    const uint32_t wd = gemv::word(v < 4 ? q0 : q1, v % 4);
-    float qn[4];
+    float qn[kM][4];
 #pragma unroll
-    for (int m = 0; m < 4; ++m)
-      qn[m] = gemv::small_int_f((wd >> (8 * m + sh)) & 15u);
+    for (int m = 0; m < kM; ++m) {
+      const uint32_t wd = gemv::word(q[m][v / 4], v % 4);
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        qn[m][e] = gemv::small_int_f((wd >> (8 * e + sh)) & 15u);
+    }
 #pragma unroll
     for (unsigned a = 0; a < kT; ++a) {
       const float4 xv = *reinterpret_cast<const float4*>(x + a * ld + 4 * v);
-      out[a] += qn[0] * xv.x + qn[1] * xv.y + qn[2] * xv.z + qn[3] * xv.w;
+#pragma unroll
+      for (int m = 0; m < kM; ++m)
+        out[m][a] += qn[m][0] * xv.x + qn[m][1] * xv.y + qn[m][2] * xv.z + qn[m][3] * xv.w;
     }
   }
 }
@@ -266,17 +278,16 @@ __device__ inline void moe_gate_up_grouped_op(const MoeGateUpGroupedParams& p, u
       const std::uint8_t* ublk = uw + std::size_t{kb} * 144;
       const uint4 gh = __ldg(reinterpret_cast<const uint4*>(gblk));
       const uint4 uh = __ldg(reinterpret_cast<const uint4*>(ublk));
+      const std::uint8_t* const qs[2] = {gblk + 16, ublk + 16};
       for (unsigned j = 0; j < 8; ++j) {
-        float q[kT];
+        float q[2][kT];
         const float2 gs = moe_detail::q4k_sub_scale(gh, j), us = moe_detail::q4k_sub_scale(uh, j);
-        moe_detail::q4k_sub_dot<kT>(gblk + 16, j, &xs[0][32 * j], 256, q);
+        moe_detail::q4k_sub_dot<kT, 2>(qs, j, &xs[0][32 * j], 256, q);
 #pragma unroll
-        for (unsigned a = 0; a < kT; ++a)
-          ga[a] += gs.x * q[a] - gs.y * xsum[a][j];
-        moe_detail::q4k_sub_dot<kT>(ublk + 16, j, &xs[0][32 * j], 256, q);
-#pragma unroll
-        for (unsigned a = 0; a < kT; ++a)
-          ua[a] += us.x * q[a] - us.y * xsum[a][j];
+        for (unsigned a = 0; a < kT; ++a) {
+          ga[a] += gs.x * q[0][a] - gs.y * xsum[a][j];
+          ua[a] += us.x * q[1][a] - us.y * xsum[a][j];
+        }
       }
     }
 #pragma unroll
@@ -357,14 +368,15 @@ __device__ inline void moe_down_grouped_op(const MoeDownGroupedParams& p, unsign
       for (unsigned b = 0; b < K / 256; ++b) {
         const std::uint8_t* blk = w + std::size_t{b} * 144;
         const uint4 h = __ldg(reinterpret_cast<const uint4*>(blk));
+        const std::uint8_t* const qs[1] = {blk + 16};
         for (unsigned j = 0; j < 8; ++j) {
-          float q[kT];
-          moe_detail::q4k_sub_dot<kT>(blk + 16, j, &hs[0][256 * b + 32 * j], K, q);
+          float q[1][kT];
+          moe_detail::q4k_sub_dot<kT, 1>(qs, j, &hs[0][256 * b + 32 * j], K, q);
           const float2 sm = moe_detail::q4k_sub_scale(h, j);
           const unsigned g16 = (256 * b + 32 * j) / 16;
 #pragma unroll
           for (unsigned a = 0; a < kT; ++a)
-            acc[a] += sm.x * q[a] - sm.y * (hsum[a][g16] + hsum[a][g16 + 1]);
+            acc[a] += sm.x * q[0][a] - sm.y * (hsum[a][g16] + hsum[a][g16 + 1]);
         }
       }
     } else {

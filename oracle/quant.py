@@ -119,6 +119,42 @@ def q6k_repack_r1(raw: np.ndarray, k: int) -> np.ndarray:
     return out
 
 
+def q4k_r1_to_gguf(raw: np.ndarray) -> np.ndarray:
+    """Q4_K r1 bytes -> GGUF Q4_K bytes: the 24-bit fields back into the 12-byte 6-bit packing
+    (j < 4: scale / min in the low 6 bits of bytes j / j + 4; j >= 4: low nibbles in byte j + 4,
+    top 2 bits in the high bits of bytes j - 4 / j)."""
+    raw = np.ascontiguousarray(raw, np.uint8)
+    b = raw.copy().reshape(-1, Q4K_BYTES)
+    f = b[:, 4:16].astype(np.uint32).reshape(-1, 4, 3)
+    v = f[:, :, 0] | f[:, :, 1] << 8 | f[:, :, 2] << 16
+    sc = np.empty((b.shape[0], 8), np.uint32)
+    mn = np.empty_like(sc)
+    sc[:, 0::2], mn[:, 0::2] = v & 63, (v >> 6) & 63
+    sc[:, 1::2], mn[:, 1::2] = (v >> 12) & 63, (v >> 18) & 63
+    q = np.zeros((b.shape[0], 12), np.uint32)
+    for j in range(4):
+        q[:, j] |= sc[:, j]
+        q[:, j + 4] |= mn[:, j]
+    for j in range(4, 8):
+        q[:, j + 4] = (sc[:, j] & 0xF) | (mn[:, j] & 0xF) << 4
+        q[:, j - 4] |= (sc[:, j] >> 4) << 6
+        q[:, j] |= (mn[:, j] >> 4) << 6
+    b[:, 4:16] = q.astype(np.uint8)
+    return b.reshape(raw.shape)
+
+
+def q6k_r1_to_gguf(rows: np.ndarray, k: int) -> np.ndarray:
+    """Q6_K r1 rows [rows][row_bytes] -> GGUF Q6_K rows [rows][k / 256 * 210]."""
+    nb = k // 256
+    rows = np.ascontiguousarray(rows, np.uint8).reshape(-1, q6k_r1_row_bytes(k))
+    out = np.empty((rows.shape[0], nb, Q6K_BYTES), np.uint8)
+    out[:, :, 0:128] = rows[:, 0:nb * 128].reshape(-1, nb, 128)
+    out[:, :, 128:192] = rows[:, nb * 128:nb * 192].reshape(-1, nb, 64)
+    out[:, :, 192:208] = rows[:, nb * 192:nb * 208].reshape(-1, nb, 16)
+    out[:, :, 208:210] = rows[:, nb * 208:nb * 210].reshape(-1, nb, 2)
+    return out.reshape(rows.shape[0], -1)
+
+
 def random_q4k(rng: np.random.RandomState, rows: int, k: int, d_scale: float = 2e-3) -> np.ndarray:
     """Random GGUF Q4_K rows [rows][k / 256 * 144]: random codes and 6-bit scales / mins, d and
     dmin drawn around d_scale (positive FP16)."""
@@ -143,13 +179,15 @@ def act_fp16(x: np.ndarray) -> np.ndarray:
 
 
 def act_int8(x: np.ndarray) -> np.ndarray:
-    """The INT8 activation format: per 32 consecutive values q = rint(x * 127 / amax), x' = q * amax
-    / 127 (0 where amax = 0), as float64."""
-    x = np.asarray(x, np.float64).reshape(-1, 32)
+    """The INT8 activation format: per 32 consecutive values amax = max |x|, q = rint((x * 127) /
+    amax), x' = q * (amax / 127) (0 where amax = 0), each operation in FP32 as the kernels round
+    it; returned as float64."""
+    x = np.asarray(x, np.float32).reshape(-1, 32)
     amax = np.abs(x).max(axis=1, keepdims=True)
-    with np.errstate(invalid="ignore", divide="ignore"):
-        q = np.where(amax > 0, np.rint(x * 127.0 / amax), 0.0)
-    return (q * amax / 127.0).reshape(-1)
+    safe = np.where(amax > 0, amax, np.float32(1))
+    q = np.rint((x * np.float32(127)) / safe).astype(np.float32)
+    xq = np.where(amax > 0, q * (safe / np.float32(127)), np.float32(0)).astype(np.float32)
+    return xq.reshape(-1).astype(np.float64)
 
 
 def gemv(w: np.ndarray, x_act: np.ndarray) -> np.ndarray:

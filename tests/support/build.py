@@ -1,4 +1,5 @@
-"""Builds tests/support/libmiso_test_support.so (test-only kernels; see combine_variants.cu)."""
+"""Builds tests/support/libmiso_test_support.so (test-only kernels and launchers: combine_variants.cu,
+engine_kernels.cu)."""
 import os
 import subprocess
 import sys
@@ -18,18 +19,18 @@ def _product_build():
 _b = _product_build()
 
 LIB = os.path.join(HERE, "libmiso_test_support.so")
-SRC = os.path.join(HERE, "combine_variants.cu")
+SRCS = [os.path.join(HERE, "combine_variants.cu"), os.path.join(HERE, "engine_kernels.cu")]
 
 
 def build(force: bool = False) -> str:
-    deps = [SRC] + [os.path.join(_b.CSRC, "kernels", f) for f in os.listdir(
+    deps = SRCS + [os.path.join(_b.CSRC, "kernels", f) for f in os.listdir(
         os.path.join(_b.CSRC, "kernels"))]
     if not force and os.path.exists(LIB) and all(
             os.path.getmtime(d) <= os.path.getmtime(LIB) for d in deps):
         return LIB
     cmd = [os.environ.get("NVCC", "nvcc"), *[f for f in _b.NVCC_FLAGS if f != "-warn-spills"
                                              and f != "-Xptxas"],
-           f"-I{_b.CSRC}", "-o", LIB, SRC]
+           f"-I{_b.CSRC}", "-o", LIB, *SRCS]
     subprocess.run(cmd, check=True)
     return LIB
 
