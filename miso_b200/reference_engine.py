@@ -56,6 +56,13 @@ NOT_BUILT = {
     "test_deltanet_prepare": "includes bench/deltanet/activation_prepare.hpp, gfx906 DPP code",
 }
 
+# Model-level test programs that compare the engine with itself (prefill vs token-by-token decode,
+# fused vs separate GEMVs, staged vs plain uploads). They are built a second time, into
+# bin/synthetic/, reading a synthetic model with the reference model's architecture and tensor
+# layout (tests/support/synthetic_model.py writes it to <out>/../synthetic_model/ where these
+# paths point).
+SYNTHETIC_TESTS = ["test_prefill", "test_fused_gemv", "test_gemv_dispatch", "test_load_stage"]
+
 # The model file the GGUF-gated test cases look for (the reference's CMake default,
 # CMakeLists.txt:83-85). Those cases skip themselves when it is absent.
 DEFAULT_GGUF = os.environ.get(
@@ -81,8 +88,14 @@ def _stamp(ref: Path) -> str:
         if p.is_file():
             h.update(str(p.relative_to(ref)).encode())
             h.update(p.read_bytes())
-    h.update(" ".join(NVCC_FLAGS + [DEFAULT_GGUF]).encode())
+    h.update(" ".join(NVCC_FLAGS + [DEFAULT_GGUF] + SYNTHETIC_TESTS).encode())
     return h.hexdigest()
+
+
+def synthetic_paths(out: Path = DEFAULT_OUT) -> dict[str, Path]:
+    """Where the synthetic model and its prompt file live for the bin/synthetic/ programs."""
+    base = Path(out).resolve().parent / "synthetic_model"
+    return {"dir": base, "model": base / "model.gguf", "golden": base / "golden"}
 
 
 def build(ref: str | Path, out: str | Path = DEFAULT_OUT, jobs: int | None = None,
@@ -95,6 +108,10 @@ def build(ref: str | Path, out: str | Path = DEFAULT_OUT, jobs: int | None = Non
     obj.mkdir(parents=True, exist_ok=True)
     binp.mkdir(parents=True, exist_ok=True)
     targets = {name: binp / name for name in list(TESTS) + ["miso"]}
+    targets.update({f"synthetic/{name}": binp / "synthetic" / name for name in SYNTHETIC_TESTS})
+    (binp / "synthetic").mkdir(exist_ok=True)
+    (obj / "synthetic").mkdir(exist_ok=True)
+    synth = synthetic_paths(out)
     stamp = _stamp(ref)
     stamp_file = out / "stamp"
     if stamp_file.exists() and stamp_file.read_text() == stamp and \
@@ -125,6 +142,14 @@ def build(ref: str | Path, out: str | Path = DEFAULT_OUT, jobs: int | None = Non
         for src in srcs:
             compiles.append((Path(src).stem, nvcc + ["-c", str(ref / "tests" / src),
                                                      "-o", str(obj / f"{Path(src).stem}.o")]))
+    nvcc_synth = ["nvcc"] + NVCC_FLAGS + ["-x", "cu"] + inc + [
+        f'-DMISO_FIXTURE_DIR="{ref / "tests" / "fixtures"}"',
+        f'-DMISO_GOLDEN_DIR="{synth["golden"]}"', f'-DMISO_ORNITH_GGUF="{synth["model"]}"']
+    for name in SYNTHETIC_TESTS:
+        for src in TESTS[name][0]:
+            compiles.append((f"synthetic/{Path(src).stem}",
+                             nvcc_synth + ["-c", str(ref / "tests" / src), "-o",
+                                           str(obj / "synthetic" / f"{Path(src).stem}.o")]))
 
     with cf.ThreadPoolExecutor(max_workers=jobs or os.cpu_count() or 4) as ex:
         results = list(ex.map(lambda c: (c[0], _run(c[1])), compiles))
@@ -142,6 +167,12 @@ def build(ref: str | Path, out: str | Path = DEFAULT_OUT, jobs: int | None = Non
         objs = [str(obj / f"{Path(s).stem}.o") for s in srcs] + [str(obj / "test_main.o")]
         links.append((name, link + ["-o", str(targets[name])] + objs +
                       (engine if with_engine else []) + host))
+    for name in SYNTHETIC_TESTS:
+        srcs, with_engine = TESTS[name]
+        objs = [str(obj / "synthetic" / f"{Path(s).stem}.o") for s in srcs] + \
+            [str(obj / "test_main.o")]
+        links.append((f"synthetic/{name}", link + ["-o", str(targets[f"synthetic/{name}"])] +
+                      objs + (engine if with_engine else []) + host))
     with cf.ThreadPoolExecutor(max_workers=jobs or os.cpu_count() or 4) as ex:
         results = list(ex.map(lambda c: (c[0], _run(c[1])), links))
     for name, (rc, log) in results:

@@ -17,7 +17,8 @@ def built():
 
 def test_engine_cli_and_tests_build(built):
     recipe = rp.recipe()
-    assert set(built) == set(recipe.TESTS) | {"miso"}
+    assert set(built) == set(recipe.TESTS) | {"miso"} | \
+        {f"synthetic/{n}" for n in recipe.SYNTHETIC_TESTS}
     for name, path in built.items():
         assert path.exists() and path.stat().st_size > 0, name
     # Targets the SURVEY asks for first: the three engine-level tests.
@@ -25,7 +26,8 @@ def test_engine_cli_and_tests_build(built):
         assert name in built
 
 
-@pytest.mark.parametrize("name", sorted(rp.recipe().TESTS))
+@pytest.mark.parametrize("name", sorted(rp.recipe().TESTS) +
+                         [f"synthetic/{n}" for n in rp.recipe().SYNTHETIC_TESTS])
 def test_program_lists_its_cases(built, name):
     rc, out, _ = rp.run(name, ["--list-test-cases"], timeout=60)
     assert rc == 0, out[-2000:]
