@@ -21,7 +21,7 @@ def test_engine_cli_and_tests_build(built):
         {f"synthetic/{n}" for n in recipe.SYNTHETIC_TESTS}
     for name, path in built.items():
         assert path.exists() and path.stat().st_size > 0, name
-    # Targets the SURVEY asks for first: the three engine-level tests.
+    # The engine-level tests that link the whole engine library.
     for name in ("test_attention", "test_deltanet", "test_prefill"):
         assert name in built
 
