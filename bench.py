@@ -187,7 +187,9 @@ def run_miso(args) -> None:
     from miso_b200 import capi
 
     lens0 = lens_config()
-    extra = args.warmup + 2 * args.steps + 4  # room for the appended tokens
+    # Room for the appended tokens: the device-timed loop and the end-to-end loop each append
+    # warmup + steps tokens to every sequence.
+    extra = 2 * (args.warmup + args.steps) + 4
     caps = (lens0.astype(np.int64) + extra)
     seg_caps = np.repeat(caps, KV_HEADS)
     starts = np.concatenate([[0], np.cumsum(seg_caps)[:-1]]).astype(np.int64)
@@ -222,9 +224,10 @@ def run_miso(args) -> None:
                    capi.load().miso_attn_prep_batched(ctypes.byref(p),
                                                       stream.cuda_stream))
 
-    def decode(qg_base: int):
+    def decode(qg_base: int, out=None):
+        out = core if out is None else out
         dp = capi.AttnDecodeParams(q.data_ptr(), qg_base, pool.k.data_ptr(), pool.v.data_ptr(),
-                                   pool.kv_row.data_ptr(), pool.lens.data_ptr(), core.data_ptr(),
+                                   pool.kv_row.data_ptr(), pool.lens.data_ptr(), out.data_ptr(),
                                    rows, BATCH, PROJ)
         capi.check("miso_attn_decode",
                    capi.load().miso_attn_decode(ctypes.byref(dp),
@@ -275,26 +278,59 @@ def run_miso(args) -> None:
     pk = peaks()
 
     # ---- end to end through the C ABI with host buffers ---------------------------------------
-    host_in = torch.randn((BATCH, PROJ), dtype=torch.float32).pin_memory()
-    host_out = torch.empty((BATCH, Q_HEADS, DIM), dtype=torch.float32).pin_memory()
-    dev_in = torch.empty((BATCH, PROJ), device=dev)
-    for _ in range(args.warmup):
-        dev_in.copy_(host_in, non_blocking=True)
-        step(dev_in.data_ptr())
-        decode(dev_in.data_ptr())
-        host_out.copy_(core, non_blocking=True)
+    # A serving loop: every step's inputs are uploaded from pinned host memory and its output is
+    # downloaded to pinned host memory, inside the timed region. Inputs and outputs are double
+    # buffered and the copies run on their own streams, so the upload of step i + 1 and the
+    # download of step i overlap step i's kernels; events order every reuse of a buffer.
+    host_in = [torch.randn((BATCH, PROJ), dtype=torch.float32).pin_memory() for _ in range(2)]
+    host_out = [torch.empty((BATCH, Q_HEADS, DIM), dtype=torch.float32).pin_memory()
+                for _ in range(2)]
+    dev_in = [torch.empty((BATCH, PROJ), device=dev) for _ in range(2)]
+    dev_out = [torch.empty((BATCH, Q_HEADS, DIM), device=dev) for _ in range(2)]
+    h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
+    def serve(n: int) -> None:
+        uploaded = [torch.cuda.Event() for _ in range(2)]    # input b is on the device
+        consumed = [torch.cuda.Event() for _ in range(2)]    # step using buffer b has finished
+        downloaded = [torch.cuda.Event() for _ in range(2)]  # output b is in host memory
+        t0 = torch.cuda.Event()
+        t0.record(stream)
+        h2d.wait_event(t0)
+        with torch.cuda.stream(h2d):
+            dev_in[0].copy_(host_in[0], non_blocking=True)
+        uploaded[0].record(h2d)
+        for i in range(n):
+            b = i % 2
+            if i + 1 < n:  # upload the next step's input while this step computes
+                if i >= 1:
+                    h2d.wait_event(consumed[1 - b])
+                with torch.cuda.stream(h2d):
+                    dev_in[1 - b].copy_(host_in[1 - b], non_blocking=True)
+                uploaded[1 - b].record(h2d)
+            stream.wait_event(uploaded[b])
+            if i >= 2:
+                stream.wait_event(downloaded[b])  # step i - 2's output has left buffer b
+            step(dev_in[b].data_ptr())
+            decode(dev_in[b].data_ptr(), dev_out[b])
+            consumed[b].record(stream)
+            d2h.wait_event(consumed[b])
+            with torch.cuda.stream(d2h):
+                host_out[b].copy_(dev_out[b], non_blocking=True)
+            downloaded[b].record(d2h)
+        for b in range(min(n, 2)):
+            stream.wait_event(downloaded[b])
+
+    serve(args.warmup)
     barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(args.steps):
-        dev_in.copy_(host_in, non_blocking=True)
-        step(dev_in.data_ptr())
-        decode(dev_in.data_ptr())
-        host_out.copy_(core, non_blocking=True)
+    serve(args.steps)
     e1.record(stream)
     torch.cuda.synchronize()
     barrier()
+    last = (args.steps - 1) % 2  # the last step's output reached host memory intact
+    assert torch.equal(host_out[last], dev_out[last].cpu()), "end-to-end download mismatch"
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
 
     prefill = None if args.no_prefill else bench_prefill(args, dev, stream, max_over_ranks,
