@@ -202,6 +202,22 @@ int miso_attn_prefill(const miso_attn_prefill_params* p, void* stream);
 int miso_deltanet_step(const miso_deltanet_step_params* p, void* stream);
 /* deltanet_seq_kernel<256><<<32, 256>>>, src/engine/deltanet.hip:113. */
 int miso_deltanet_seq(const miso_deltanet_seq_params* p, void* stream);
+
+/* Speculative (multi-token prediction) verification of p->n draft tokens through a DeltaNet
+ * layer, for the reference's planned commit / rollback of a variable number of accepted tokens
+ * (docs/decisions/ADR_002-build-scope-numerics-ops.md D8). Same recurrence and outputs p->out as
+ * miso_deltanet_seq, bit for bit, but p->state and p->conv_out are NOT written (p->conv_out may be
+ * NULL); instead the state after token t goes to state_ckpt + t * 32*128*128 floats (16-byte
+ * aligned) and the conv history after token t to conv_ckpt + t * 8192*3 floats.
+ * miso_deltanet_commit then keeps the first k_accepted tokens: it copies checkpoint
+ * k_accepted - 1 into state and conv_out (bitwise what miso_deltanet_seq over those tokens leaves;
+ * flip the caller's conv parity as after miso_deltanet_seq), and for k_accepted == 0 changes
+ * nothing. The KV side of a rollback is the cache length: set it to its pre-verification value
+ * plus k_accepted. Errors: MISO_ERR_INVALID for NULL pointers or k_accepted > n. */
+int miso_deltanet_seq_ckpt(const miso_deltanet_seq_params* p, float* state_ckpt,
+                           float* conv_ckpt, void* stream);
+int miso_deltanet_commit(const float* state_ckpt, const float* conv_ckpt, unsigned n,
+                         unsigned k_accepted, float* state, float* conv_out, void* stream);
 /* deltanet_conv_kernel<<<32, 256>>>, tests/test_deltanet_chunk.hip:82. */
 int miso_deltanet_conv(const miso_deltanet_conv_params* p, void* stream);
 /* deltanet_norm_kernel<<<64, 256>>>, tests/test_deltanet_chunk.hip:83. */

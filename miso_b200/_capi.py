@@ -100,6 +100,8 @@ SIGNATURES = {
     "miso_attn_prefill": (C.c_int, [C.POINTER(AttnPrefillParams), _P]),
     "miso_deltanet_step": (C.c_int, [C.POINTER(DeltaNetStepParams), _P]),
     "miso_deltanet_seq": (C.c_int, [C.POINTER(DeltaNetSeqParams), _P]),
+    "miso_deltanet_seq_ckpt": (C.c_int, [C.POINTER(DeltaNetSeqParams), _P, _P, _P]),
+    "miso_deltanet_commit": (C.c_int, [_P, _P, C.c_uint, C.c_uint, _P, _P, _P]),
     "miso_deltanet_conv": (C.c_int, [C.POINTER(DeltaNetConvParams), _P]),
     "miso_deltanet_norm": (C.c_int, [C.POINTER(DeltaNetConvParams), _P]),
     "miso_deltanet_chunk": (C.c_int, [C.POINTER(DeltaNetChunkParams), _P]),

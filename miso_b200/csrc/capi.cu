@@ -286,6 +286,35 @@ int miso_deltanet_seq(const miso_deltanet_seq_params* p, void* stream) {
   return launch_status();
 }
 
+int miso_deltanet_seq_ckpt(const miso_deltanet_seq_params* p, float* state_ckpt,
+                           float* conv_ckpt, void* stream) {
+  if (p == nullptr || p->qkv == nullptr || p->z == nullptr || p->a == nullptr ||
+      p->b == nullptr || p->conv_w == nullptr || p->conv_in == nullptr || p->ssm_a == nullptr ||
+      p->dt_bias == nullptr || p->norm_w == nullptr || p->state == nullptr || p->out == nullptr ||
+      state_ckpt == nullptr || conv_ckpt == nullptr || !aligned16(p->state) ||
+      !aligned16(state_ckpt))
+    return MISO_ERR_INVALID;
+  k::deltanet_seq_ckpt_kernel<256><<<32, 256, 0, as_stream(stream)>>>(
+      *reinterpret_cast<const k::DeltaNetSeqParams*>(p), state_ckpt, conv_ckpt);
+  return launch_status();
+}
+
+int miso_deltanet_commit(const float* state_ckpt, const float* conv_ckpt, unsigned n,
+                         unsigned k_accepted, float* state, float* conv_out, void* stream) {
+  if (state_ckpt == nullptr || conv_ckpt == nullptr || state == nullptr || conv_out == nullptr ||
+      k_accepted > n)
+    return MISO_ERR_INVALID;
+  if (k_accepted == 0)
+    return 0;
+  const std::size_t sf = std::size_t{32} * 128 * 128, cf = std::size_t{8192} * 3;
+  cudaError_t e = cudaMemcpyAsync(state, state_ckpt + (k_accepted - 1) * sf, sf * sizeof(float),
+                                  cudaMemcpyDeviceToDevice, as_stream(stream));
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(conv_out, conv_ckpt + (k_accepted - 1) * cf, cf * sizeof(float),
+                        cudaMemcpyDeviceToDevice, as_stream(stream));
+  return static_cast<int>(e);
+}
+
 int miso_deltanet_conv(const miso_deltanet_conv_params* p, void* stream) {
   if (p == nullptr || p->qkv == nullptr || p->conv_w == nullptr || p->conv_in == nullptr ||
       p->conv_out == nullptr || p->q == nullptr || p->k == nullptr || p->v == nullptr)

@@ -229,11 +229,27 @@ struct DeltaNetSeqParams {
   unsigned qkv_stride;  // 8192, or larger when qkv shares a buffer with z_ab
 };
 
+namespace dn_detail {
+
+// Where a sequence writes its results. state / conv: the final state (in place) and conv history
+// (conv_out), or null to leave them untouched. state_ckpt / conv_ckpt: the state
+// [n][32][128][128] and conv history [n][8192][3] after every token, or null. Both forms share one
+// body, so checkpoints carry exactly the bits a shorter sequence would leave.
+struct SeqSinks {
+  float* state;
+  float* conv;
+  float* state_ckpt;
+  float* conv_ckpt;
+};
+
 template <int kBlock>
-__device__ void deltanet_seq_op(const DeltaNetSeqParams& p, unsigned first, unsigned count) {
+__device__ void seq_body(const DeltaNetSeqParams& p, const SeqSinks& out, unsigned first,
+                         unsigned count) {
   using namespace deltanet_detail;
   static_assert(kBlock == 2 * kDim, "eight warps of 16 state rows each");
   constexpr unsigned kOut = kVHeads * kDim;
+  constexpr std::size_t kStateFloats = std::size_t{kVHeads} * kDim * kDim;
+  constexpr std::size_t kConvFloats = std::size_t{3} * (2 * kKHeads + kVHeads) * kDim;
   __shared__ dn_detail::TokenShared sh;
   const unsigned t = threadIdx.x;
   for (unsigned h = first + blockIdx.x; h < first + count; h += gridDim.x) {
@@ -249,7 +265,7 @@ __device__ void deltanet_seq_op(const DeltaNetSeqParams& p, unsigned first, unsi
 #pragma unroll
     for (int i = 0; i < 3; ++i)
       h0[i] = p.conv_in[3 * c0 + i], h1[i] = p.conv_in[3 * c1 + i];
-    float* S = p.state + std::size_t{h} * kDim * kDim;
+    const float* S = p.state + std::size_t{h} * kDim * kDim;
     float4 s[16];
     dn_detail::load_state(s, S);
     for (unsigned tok = 0; tok < p.n; ++tok) {
@@ -269,20 +285,63 @@ __device__ void deltanet_seq_op(const DeltaNetSeqParams& p, unsigned first, unsi
       dn_detail::token_update(sh, s, p.b[zrow + h], p.a[zrow + h], p.ssm_a[h], p.dt_bias[h],
                               p.norm_w, p.z + zrow + h * kDim, p.eps,
                               p.out + std::size_t{tok} * kOut + h * kDim);
-    }
-    dn_detail::store_state(s, S);
-    if (own_qk) {
+      if (out.state_ckpt != nullptr)
+        dn_detail::store_state(s, out.state_ckpt + tok * kStateFloats + std::size_t{h} * kDim * kDim);
+      if (out.conv_ckpt != nullptr) {
+        float* cc = out.conv_ckpt + tok * kConvFloats;
+        if (own_qk) {
 #pragma unroll
-      for (int i = 0; i < 3; ++i)
-        p.conv_out[3 * c0 + i] = h0[i];
-    }
-    if (t < kDim) {
+          for (int i = 0; i < 3; ++i)
+            cc[3 * c0 + i] = h0[i];
+        }
+        if (t < kDim) {
 #pragma unroll
-      for (int i = 0; i < 3; ++i)
-        p.conv_out[3 * c1 + i] = h1[i];
+          for (int i = 0; i < 3; ++i)
+            cc[3 * c1 + i] = h1[i];
+        }
+      }
+    }
+    if (out.state != nullptr)
+      dn_detail::store_state(s, out.state + std::size_t{h} * kDim * kDim);
+    if (out.conv != nullptr) {
+      if (own_qk) {
+#pragma unroll
+        for (int i = 0; i < 3; ++i)
+          out.conv[3 * c0 + i] = h0[i];
+      }
+      if (t < kDim) {
+#pragma unroll
+        for (int i = 0; i < 3; ++i)
+          out.conv[3 * c1 + i] = h1[i];
+      }
     }
     __syncthreads();
   }
+}
+
+}  // namespace dn_detail
+
+template <int kBlock>
+__device__ void deltanet_seq_op(const DeltaNetSeqParams& p, unsigned first, unsigned count) {
+  dn_detail::seq_body<kBlock>(p, {p.state, p.conv_out, nullptr, nullptr}, first, count);
+}
+
+// Speculative verification (multi-token prediction): the same n-token recurrence and outputs as
+// deltanet_seq_op, but p.state and p.conv_out are left untouched; the state and conv history
+// after every token go to state_ckpt [n][32][128][128] and conv_ckpt [n][8192][3] instead, so a
+// caller can commit any prefix of k accepted tokens by taking checkpoint k - 1 (bitwise what
+// deltanet_seq_op would leave after those k tokens) and reject the rest by taking nothing.
+template <int kBlock>
+__device__ void deltanet_seq_ckpt_op(const DeltaNetSeqParams& p, float* state_ckpt,
+                                     float* conv_ckpt, unsigned first, unsigned count) {
+  dn_detail::seq_body<kBlock>(p, {nullptr, nullptr, state_ckpt, conv_ckpt}, first, count);
+}
+
+template <int kBlock>
+__global__ void __launch_bounds__(kBlock) deltanet_seq_ckpt_kernel(DeltaNetSeqParams p,
+                                                                   float* state_ckpt,
+                                                                   float* conv_ckpt) {
+  deltanet_seq_ckpt_op<kBlock>(p, state_ckpt, conv_ckpt, 0, deltanet_detail::kVHeads);
 }
 
 template <int kBlock>

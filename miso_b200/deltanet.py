@@ -80,3 +80,46 @@ def deltanet_prefill_core(st: DeltaNetState, proj: torch.Tensor, n: int, conv_w,
     seq(p, stream)
     st.parity = 1 - st.parity
     return out
+
+
+class DraftCheckpoints:
+    """Per-token state / conv-history checkpoints of a speculative verification pass of up to
+    max_tokens draft tokens (multi-token prediction: the reference's planned commit / rollback of
+    2-4 accepted tokens, docs/decisions/ADR_002-build-scope-numerics-ops.md D8)."""
+
+    def __init__(self, max_tokens: int, device="cuda"):
+        self.max_tokens = max_tokens
+        self.state = torch.empty((max_tokens, V_HEADS, DIM, DIM), dtype=torch.float32,
+                                 device=device)
+        self.conv = torch.empty((max_tokens, CHANNELS, 3), dtype=torch.float32, device=device)
+        self.n = 0
+
+
+def deltanet_verify_core(st: DeltaNetState, ck: DraftCheckpoints, proj: torch.Tensor, n: int,
+                         conv_w, ssm_a, dt_bias, norm_w, out: torch.Tensor, eps: float,
+                         stream=None) -> torch.Tensor:
+    """n draft tokens from a [n][12352] projection buffer: outputs as deltanet_prefill_core, the
+    layer state left as it was and checkpoints taken after every token."""
+    if not 0 < n <= ck.max_tokens:
+        raise ValueError(f"verify: {n} tokens, checkpoints hold {ck.max_tokens}")
+    base = proj.data_ptr()
+    z = base + 8192 * 4
+    p = capi.DeltaNetSeqParams(base, z, z + 4096 * 4, z + 4128 * 4, _ptr(conv_w),
+                               _ptr(st.conv[st.parity]), None, _ptr(ssm_a), _ptr(dt_bias),
+                               _ptr(norm_w), _ptr(st.s), _ptr(out), n, eps, PROJ, PROJ)
+    capi.check("miso_deltanet_seq_ckpt",
+               capi.load().miso_deltanet_seq_ckpt(C.byref(p), _ptr(ck.state), _ptr(ck.conv),
+                                                  _stream(stream)))
+    ck.n = n
+    return out
+
+
+def deltanet_commit(st: DeltaNetState, ck: DraftCheckpoints, k_accepted: int,
+                    stream=None) -> None:
+    """Keeps the first k_accepted verified tokens (0 keeps the state from before the pass)."""
+    capi.check("miso_deltanet_commit",
+               capi.load().miso_deltanet_commit(_ptr(ck.state), _ptr(ck.conv), ck.n, k_accepted,
+                                                _ptr(st.s), _ptr(st.conv[1 - st.parity]),
+                                                _stream(stream)))
+    if k_accepted > 0:
+        st.parity = 1 - st.parity

@@ -121,6 +121,16 @@ def test_invalid_arguments_are_rejected_without_a_device():
     assert lib.miso_deltanet_prefill_tc(C.byref(dp), fake, 1024, None) == -2
     for stage in (lib.miso_deltanet_prefill_tc_front, lib.miso_deltanet_prefill_tc_recur):
         assert stage(C.byref(dp), fake, 1024, None) == -2  # the same scratch contract
+    # Speculative verification: checkpoints are required; commit refuses k_accepted > n and null
+    # buffers, and with k_accepted = 0 it leaves everything as it was (no device work).
+    assert lib.miso_deltanet_seq_ckpt(None, fake, fake, None) == -1
+    assert lib.miso_deltanet_seq_ckpt(C.byref(dp), None, fake, None) == -1
+    assert lib.miso_deltanet_seq_ckpt(C.byref(dp), fake, None, None) == -1
+    assert lib.miso_deltanet_seq_ckpt(C.byref(dp), fake + 4, fake, None) == -1  # unaligned
+    assert lib.miso_deltanet_commit(fake, fake, 3, 4, fake, fake, None) == -1
+    assert lib.miso_deltanet_commit(None, fake, 3, 1, fake, fake, None) == -1
+    assert lib.miso_deltanet_commit(fake, fake, 3, 1, fake, None, None) == -1
+    assert lib.miso_deltanet_commit(fake, fake, 3, 0, fake, fake, None) == 0
     st = C.c_int(0)
     assert lib.miso_device_status(0, None) == -1
     assert st.value == 0
