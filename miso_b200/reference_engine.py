@@ -46,6 +46,13 @@ TESTS = {
     "test_load_stage": (["test_load_stage.hip"], True),
 }
 
+# The reference's per-layer decode benchmarks (bench/CMakeLists.txt:12-35): name -> source under
+# bench/. Both take the model file as their first argument.
+BENCHES = {
+    "bench_attention": "attention/bench_attention.hip",
+    "bench_deltanet": "deltanet/bench_deltanet.hip",
+}
+
 # Test programs of the reference that are not built, and why.
 NOT_BUILT = {
     "test_device": "reads hipDeviceProp_t::gcnArchName, an AMD-only device property",
@@ -84,11 +91,11 @@ def _stamp(ref: Path) -> str:
             h.update(p.name.encode())
             h.update(p.read_bytes())
     for p in sorted((ref / "src").rglob("*")) + sorted((ref / "tests").glob("*.h*")) + \
-            sorted((ref / "tests").glob("*.cpp")):
+            sorted((ref / "tests").glob("*.cpp")) + [ref / "bench" / s for s in BENCHES.values()]:
         if p.is_file():
             h.update(str(p.relative_to(ref)).encode())
             h.update(p.read_bytes())
-    h.update(" ".join(NVCC_FLAGS + [DEFAULT_GGUF] + SYNTHETIC_TESTS).encode())
+    h.update(" ".join(NVCC_FLAGS + [DEFAULT_GGUF] + SYNTHETIC_TESTS + list(BENCHES)).encode())
     return h.hexdigest()
 
 
@@ -109,6 +116,7 @@ def build(ref: str | Path, out: str | Path = DEFAULT_OUT, jobs: int | None = Non
     binp.mkdir(parents=True, exist_ok=True)
     targets = {name: binp / name for name in list(TESTS) + ["miso"]}
     targets.update({f"synthetic/{name}": binp / "synthetic" / name for name in SYNTHETIC_TESTS})
+    targets.update({name: binp / name for name in BENCHES})
     (binp / "synthetic").mkdir(exist_ok=True)
     (obj / "synthetic").mkdir(exist_ok=True)
     synth = synthetic_paths(out)
@@ -142,6 +150,9 @@ def build(ref: str | Path, out: str | Path = DEFAULT_OUT, jobs: int | None = Non
         for src in srcs:
             compiles.append((Path(src).stem, nvcc + ["-c", str(ref / "tests" / src),
                                                      "-o", str(obj / f"{Path(src).stem}.o")]))
+    for name, src in BENCHES.items():
+        compiles.append((name, nvcc + ["-c", str(ref / "bench" / src), "-o",
+                                       str(obj / f"{name}.o")]))
     nvcc_synth = ["nvcc"] + NVCC_FLAGS + ["-x", "cu"] + inc + [
         f'-DMISO_FIXTURE_DIR="{ref / "tests" / "fixtures"}"',
         f'-DMISO_GOLDEN_DIR="{synth["golden"]}"', f'-DMISO_ORNITH_GGUF="{synth["model"]}"']
@@ -167,6 +178,9 @@ def build(ref: str | Path, out: str | Path = DEFAULT_OUT, jobs: int | None = Non
         objs = [str(obj / f"{Path(s).stem}.o") for s in srcs] + [str(obj / "test_main.o")]
         links.append((name, link + ["-o", str(targets[name])] + objs +
                       (engine if with_engine else []) + host))
+    for name in BENCHES:
+        links.append((name, link + ["-o", str(targets[name]), str(obj / f"{name}.o")] + engine +
+                      host))
     for name in SYNTHETIC_TESTS:
         srcs, with_engine = TESTS[name]
         objs = [str(obj / "synthetic" / f"{Path(s).stem}.o") for s in srcs] + \

@@ -61,8 +61,10 @@ def _bf16_exact(a):
     return (np.asarray(a, np.float32).view(np.uint32) & 0xFFFF0000).view(np.float32)
 
 
-def tensors(rng, vocab: int, layers: int = 4, experts: int = EXPERTS, extra: bool = True):
-    """(name, numpy shape, GGML type, data) for every tensor; quantised data as raw bytes."""
+def tensors(rng, vocab: int, layers: int = 4, experts: int = EXPERTS, extra: bool = True,
+            with_moe: bool = True):
+    """(name, numpy shape, GGML type, data) for every tensor; quantised data as raw bytes.
+    with_moe=False leaves out the MoE blocks (enough for loading single mixer layers)."""
     out = []
 
     def q(name, rows, k, t, lead=()):
@@ -117,7 +119,8 @@ def tensors(rng, vocab: int, layers: int = 4, experts: int = EXPERTS, extra: boo
             attention(i, Q6K)
         else:
             deltanet(i, Q6K)
-        moe(i)
+        if with_moe:
+            moe(i)
     if extra:
         deltanet(5, Q4K)
         attention(11, Q4K)
@@ -125,7 +128,8 @@ def tensors(rng, vocab: int, layers: int = 4, experts: int = EXPERTS, extra: boo
 
 
 def write(model_path: str, golden_dir: str, vocab: int = 8192, seed: int = 0,
-          experts: int = EXPERTS, n_prompt: int = 14, n_cont: int = 3) -> None:
+          experts: int = EXPERTS, n_prompt: int = 14, n_cont: int = 3,
+          with_moe: bool = True) -> None:
     import gguf
 
     rng = np.random.RandomState(seed)
@@ -136,7 +140,7 @@ def write(model_path: str, golden_dir: str, vocab: int = 8192, seed: int = 0,
     w.add_float32(f"{ARCH}.rope.freq_base", 10000000.0)
     w.add_uint32(f"{ARCH}.rope.dimension_count", 64)
     w.add_float32(f"{ARCH}.attention.layer_norm_rms_epsilon", 1e-6)
-    for name, shape, t, data in tensors(rng, vocab, experts=experts):
+    for name, shape, t, data in tensors(rng, vocab, experts=experts, with_moe=with_moe):
         if t == F32:
             w.add_tensor(name, data)
         else:
@@ -158,4 +162,5 @@ def write(model_path: str, golden_dir: str, vocab: int = 8192, seed: int = 0,
 
 
 if __name__ == "__main__":
-    write(sys.argv[1], sys.argv[2])
+    # synthetic_model.py <model.gguf> <golden dir> [--mixers-only]
+    write(sys.argv[1], sys.argv[2], with_moe="--mixers-only" not in sys.argv[3:])

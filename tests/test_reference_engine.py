@@ -17,7 +17,7 @@ def built():
 
 def test_engine_cli_and_tests_build(built):
     recipe = rp.recipe()
-    assert set(built) == set(recipe.TESTS) | {"miso"} | \
+    assert set(built) == set(recipe.TESTS) | {"miso"} | set(recipe.BENCHES) | \
         {f"synthetic/{n}" for n in recipe.SYNTHETIC_TESTS}
     for name, path in built.items():
         assert path.exists() and path.stat().st_size > 0, name
