@@ -45,3 +45,31 @@ def test_cli_prints_usage(built):
     import subprocess
     r = subprocess.run([str(built["miso"]), "--help"], capture_output=True, text=True, timeout=60)
     assert "usage: miso" in (r.stdout + r.stderr)
+
+
+def test_synthetic_model_matches_the_reference_models_tensor_manifest(tmp_path):
+    """The synthetic model the model-level GPU tests use has the real model's tensor names, GGML
+    types and shapes (the reference's tests/fixtures/ornith-q4km-tensors.tsv), with the expert
+    count and vocabulary scaled down here to keep the file small."""
+    gguf = pytest.importorskip("gguf")
+    manifest = rp.REFERENCE / "tests" / "fixtures" / "ornith-q4km-tensors.tsv"
+    from support import synthetic_model as S
+    S.write(str(tmp_path / "m.gguf"), str(tmp_path / "g"), vocab=512, experts=2)
+    want = {}
+    for line in manifest.read_text().splitlines():
+        if line.startswith("#"):
+            continue
+        name, ty, dims = line.split("\t")[:3]
+        want[name] = (int(ty), [int(v) for v in dims.split(",")])
+    got = {t.name: (int(t.tensor_type), [int(v) for v in t.shape])
+           for t in gguf.GGUFReader(str(tmp_path / "m.gguf")).tensors}
+    assert len(got) == 93
+    for name, (ty, dims) in got.items():
+        wt, wd = want[name]
+        if name.endswith("_exps.weight") or name.endswith("ffn_gate_inp.weight"):
+            wd = wd[:-1] + [2]
+        if name in ("token_embd.weight", "output.weight"):
+            wd = wd[:-1] + [512]
+        assert (ty, dims) == (wt, wd), name
+    g = gguf.GGUFReader(str(tmp_path / "g" / "ornith-layers.gguf"))
+    assert "golden.token_ids" in g.fields and "golden.continuation_ids" in g.fields
