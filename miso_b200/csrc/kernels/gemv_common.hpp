@@ -9,8 +9,8 @@
 //            weight = d * sc * q - dmin * m.
 //   Q6_K r1: a row of nb blocks stored as sections [ql nb*128][qh nb*64][scales nb*16][d nb*2],
 //            padded to a multiple of 16 bytes; weight = d * scale * (q - 32), q 6 bits.
-// Activations are rounded to FP16 once (the reference's FP16 activation format) and every product
-// is accumulated in FP32.
+// Activations are converted once, when a block stages them (FP16 rounding, or the per-32 absmax
+// INT8 format), and every product is accumulated in FP32.
 //
 // Work unit: a "chunk" is one 16-byte load of a row's low-bit bytes = 32 weights (16 of them from
 // the low nibbles, 16 from the high nibbles). A lane takes chunks lane, lane + 32, ... of a row,
