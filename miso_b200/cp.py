@@ -129,6 +129,61 @@ class DeltaNetWavefront:
                 self.send(layer)
 
 
+@dataclass
+class DeltaNetAffine:
+    """The same L layers and W contiguous segments as DeltaNetWavefront, with the state hand-off
+    chain replaced by per-segment affine maps. Over a segment the recurrence maps its incoming
+    state affinely, per head: S_out = A S_in + B, A a 128 x 128 matrix over the key axis that
+    depends only on the segment's keys, betas and decays. A is the segment run from S_in = I
+    with its value inputs (and their conv history) zeroed, B the segment run from S_in = 0.
+    Every rank computes its own (A, B) at once, one all-gather hands every rank all of them, each
+    rank composes its incoming state S_r = A_{r-1}(... (A_0 S_0 + B_0) ...) + B_{r-1} locally,
+    and then runs its segment from S_r for the outputs. No rank waits on another's recurrence:
+    three recurrences per segment instead of a chain of W (the wavefront's W + L - 1), at three
+    times the recurrence work.
+
+    reset / halo_recv / halo_send    the conv-history halo, as in DeltaNetWavefront
+    maps(layer, start, n)            -> (A, B) of this segment (local compute)
+    gather(layer, a, b)              -> ([A_0 .. A_{W-1}], [B_0 .. B_{W-1}]) (a collective)
+    initial(layer)                   -> S_0, the state before the sequence (the same on all ranks)
+    compose(a, s, b)                 -> a s + b, batched over the heads
+    final(layer, start, n, s)        the segment's outputs from incoming state s
+    """
+    t: int
+    world: int
+    rank: int
+    layers: int
+    maps: Callable[[int, int, int], tuple]
+    gather: Callable[[int, object, object], tuple]
+    initial: Callable[[int], object]
+    compose: Callable[[object, object, object], object]
+    final: Callable[[int, int, int, object], None]
+    reset: Callable[[int], None]
+    halo_recv: Callable[[int], None]
+    halo_send: Callable[[int], None]
+
+    def run(self) -> None:
+        start, n = contiguous_segment(self.t, self.world, self.rank)
+        if n < 3:
+            raise ValueError(f"DeltaNet segments need at least 3 tokens (t={self.t}, "
+                             f"world={self.world})")
+        last = self.rank + 1 == self.world
+        for layer in range(self.layers):
+            if self.rank == 0:
+                self.reset(layer)
+            else:
+                self.halo_recv(layer)
+            if not last:
+                self.halo_send(layer)
+        own = [self.maps(layer, start, n) for layer in range(self.layers)]
+        for layer in range(self.layers):
+            a_all, b_all = self.gather(layer, *own[layer])
+            s = self.initial(layer)
+            for r in range(self.rank):
+                s = self.compose(a_all[r], s, b_all[r])
+            self.final(layer, start, n, s)
+
+
 # ---- CUDA / NCCL bindings ----------------------------------------------------------------------
 
 ATTN_PROJ = 9216   # [q + gate 8192 | k 512 | v 512] per token

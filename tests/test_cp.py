@@ -72,6 +72,12 @@ def test_deltanet_wavefront_gloo(world):
     run_ranks("deltanet", world)
 
 
+@pytest.mark.parametrize("world", [2, 3])
+def test_deltanet_affine_schedule_gloo(world):
+    """Per-segment affine maps, all-gathered and composed, give the sequential recurrence."""
+    run_ranks("deltanet_affine", world)
+
+
 @pytest.mark.parametrize("world", [1, 2, 4])
 def test_deltanet_wavefront_call_order(world):
     """Per rank: the conv halos first (no compute behind them), then the state-independent front
@@ -107,3 +113,33 @@ def test_deltanet_wavefront_rejects_segments_shorter_than_the_conv_halo():
     wf = cp.DeltaNetWavefront(4, 2, 0, 1, noop, noop, noop, noop, noop, noop, noop)
     with pytest.raises(ValueError):
         wf.run()
+
+
+def test_deltanet_affine_composes_the_earlier_segments_in_order():
+    """Rank r composes the maps of ranks 0 .. r - 1, in order, onto the initial state, after
+    every layer's own maps were computed (no rank waits on a recurrence of another)."""
+    world, layers, t = 4, 2, 64
+    for rank in range(world):
+        log = []
+        af = cp.DeltaNetAffine(
+            t, world, rank, layers,
+            maps=lambda layer, s, n: (log.append(("maps", layer)) or (f"A{layer}", f"B{layer}")),
+            gather=lambda layer, a, b: (log.append(("gather", layer)) or
+                                        ([f"A{layer}r{r}" for r in range(world)],
+                                         [f"B{layer}r{r}" for r in range(world)])),
+            initial=lambda layer: "S0",
+            compose=lambda a, s, b: f"({a}*{s}+{b})",
+            final=lambda layer, s, n, st: log.append(("final", layer, st)),
+            reset=lambda layer: log.append(("reset", layer)),
+            halo_recv=lambda layer: log.append(("halo_recv", layer)),
+            halo_send=lambda layer: log.append(("halo_send", layer)))
+        af.run()
+        kinds = [e[0] for e in log]
+        assert kinds.index("gather") > max(i for i, k in enumerate(kinds) if k == "maps")
+        finals = [e for e in log if e[0] == "final"]
+        assert len(finals) == layers
+        for layer, (_, lay, st) in enumerate(finals):
+            want = "S0"
+            for r in range(rank):
+                want = f"(A{layer}r{r}*{want}+B{layer}r{r})"
+            assert lay == layer and st == want
