@@ -8,6 +8,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdio>
 
 // The reference spells binary16 `_Float16`. nvcc 12.9's device front end stops with "unsupported
 // float variant" on C++20 library code instantiated for _Float16 even where only host code uses it
@@ -19,8 +20,9 @@
 typedef cudaStream_t hipStream_t;
 typedef cudaError_t hipError_t;
 typedef cudaEvent_t hipEvent_t;
-typedef cudaDeviceProp hipDeviceProp_t;
 typedef cudaMemcpyKind hipMemcpyKind;
+typedef cudaGraph_t hipGraph_t;
+typedef cudaGraphExec_t hipGraphExec_t;
 
 #define hipSuccess cudaSuccess
 #define hipErrorInvalidValue cudaErrorInvalidValue
@@ -58,9 +60,15 @@ typedef cudaMemcpyKind hipMemcpyKind;
 #define hipGetErrorName cudaGetErrorName
 #define hipGetErrorString cudaGetErrorString
 #define hipGetDeviceCount cudaGetDeviceCount
-#define hipGetDeviceProperties cudaGetDeviceProperties
 #define hipSetDevice cudaSetDevice
 #define hipGetDevice cudaGetDevice
+#define hipRuntimeGetVersion cudaRuntimeGetVersion
+#define hipStreamBeginCapture cudaStreamBeginCapture
+#define hipStreamEndCapture cudaStreamEndCapture
+#define hipStreamCaptureModeGlobal cudaStreamCaptureModeGlobal
+#define hipGraphLaunch cudaGraphLaunch
+#define hipGraphDestroy cudaGraphDestroy
+#define hipGraphExecDestroy cudaGraphExecDestroy
 
 // Pinned host allocation; HIP's flags argument defaults to 0 and its default / portable / mapped
 // bits have the CUDA values.
@@ -70,6 +78,24 @@ inline cudaError_t hipHostMalloc(void** ptr, size_t size, unsigned int flags = 0
 template <class T>
 inline cudaError_t hipHostMalloc(T** ptr, size_t size, unsigned int flags = 0) {
   return cudaHostAlloc(reinterpret_cast<void**>(ptr), size, flags);
+}
+
+// Device properties: CUDA's, plus HIP's architecture-name field (here "sm_<major><minor>").
+struct hipDeviceProp_t : cudaDeviceProp {
+  char gcnArchName[256];
+};
+inline cudaError_t hipGetDeviceProperties(hipDeviceProp_t* p, int device) {
+  const cudaError_t e = cudaGetDeviceProperties(static_cast<cudaDeviceProp*>(p), device);
+  if (e == cudaSuccess)
+    std::snprintf(p->gcnArchName, sizeof p->gcnArchName, "sm_%d%d", p->major, p->minor);
+  return e;
+}
+
+// HIP keeps the older five-argument form (error node and log buffer, unused here).
+inline cudaError_t hipGraphInstantiate(hipGraphExec_t* exec, hipGraph_t graph, void* error_node,
+                                       char* log, size_t log_size) {
+  (void)error_node, (void)log, (void)log_size;
+  return cudaGraphInstantiate(exec, graph, 0);
 }
 
 // HIP's width-taking shuffles over the full warp.

@@ -30,6 +30,7 @@ ENGINE_SOURCES = ["weights", "deltanet", "attention", "moe", "model"]
 
 # Test programs built (tests/CMakeLists.txt:18-58): name -> (sources, links the engine library).
 TESTS = {
+    "test_device": (["test_device.hip"], False),
     "test_axpy": (["test_axpy.hip"], False),
     "test_attn_splitk": (["test_attn_splitk.hip"], False),
     "test_deltanet_chunk": (["test_deltanet_chunk.hip"], False),
@@ -46,16 +47,31 @@ TESTS = {
     "test_load_stage": (["test_load_stage.hip"], True),
 }
 
-# The reference's per-layer decode benchmarks (bench/CMakeLists.txt:12-35): name -> source under
-# bench/. Both take the model file as their first argument.
-BENCHES = {
-    "bench_attention": "attention/bench_attention.hip",
-    "bench_deltanet": "deltanet/bench_deltanet.hip",
+# The reference's benchmarks (bench/CMakeLists.txt:12-35): name -> source under bench/. The
+# per-layer decode benchmarks (bench_attention, bench_deltanet) take the model file as their first
+# argument.
+BENCHES = {  # name -> (source, links the engine library), as bench/CMakeLists.txt links them
+    "bench_attention": ("attention/bench_attention.hip", True),
+    "bench_deltanet": ("deltanet/bench_deltanet.hip", True),
+    "bench_combine": ("attention/bench_combine.hip", False),
+    "bench_q4k_gemv": ("gemv/bench_q4k_gemv.hip", False),
+    "bench_q6k_gemv": ("gemv/bench_q6k_gemv.hip", False),
+    "bench_qgemm": ("gemm/bench_qgemm.hip", False),
+    "bench_norm": ("norm/bench_norm.hip", False),
+    "bench_norm_chain": ("norm/bench_model_chain.hip", True),
+    "bench_moe": ("moe/bench_moe.hip", True),
+    "bench_decode": ("model/bench_decode.hip", True),
+}
+
+# Benchmarks not built, and why.
+BENCHES_NOT_BUILT = {
+    "bench_moe_coefficients": "compares against a frozen copy of the reference MoE kernel that "
+                              "uses its private q4k_detail helpers",
+    "bench_activation_prepare": "gfx906 DPP code (bench/deltanet/activation_prepare.hpp)",
 }
 
 # Test programs of the reference that are not built, and why.
 NOT_BUILT = {
-    "test_device": "reads hipDeviceProp_t::gcnArchName, an AMD-only device property",
     "test_moe": "calls the reference kernels' private helpers (kernels::moe_topk, "
                 "q4k_detail::SlotAct / load_slot) to compare against frozen copies of them",
     "test_moe_down_staging": "calls the private moe_detail::Down<> staging of the reference's "
@@ -91,7 +107,7 @@ def _stamp(ref: Path) -> str:
             h.update(p.name.encode())
             h.update(p.read_bytes())
     for p in sorted((ref / "src").rglob("*")) + sorted((ref / "tests").glob("*.h*")) + \
-            sorted((ref / "tests").glob("*.cpp")) + [ref / "bench" / s for s in BENCHES.values()]:
+            sorted((ref / "tests").glob("*.cpp")) + [ref / "bench" / s for s, _ in BENCHES.values()]:
         if p.is_file():
             h.update(str(p.relative_to(ref)).encode())
             h.update(p.read_bytes())
@@ -150,7 +166,7 @@ def build(ref: str | Path, out: str | Path = DEFAULT_OUT, jobs: int | None = Non
         for src in srcs:
             compiles.append((Path(src).stem, nvcc + ["-c", str(ref / "tests" / src),
                                                      "-o", str(obj / f"{Path(src).stem}.o")]))
-    for name, src in BENCHES.items():
+    for name, (src, _) in BENCHES.items():
         compiles.append((name, nvcc + ["-c", str(ref / "bench" / src), "-o",
                                        str(obj / f"{name}.o")]))
     nvcc_synth = ["nvcc"] + NVCC_FLAGS + ["-x", "cu"] + inc + [
@@ -178,9 +194,9 @@ def build(ref: str | Path, out: str | Path = DEFAULT_OUT, jobs: int | None = Non
         objs = [str(obj / f"{Path(s).stem}.o") for s in srcs] + [str(obj / "test_main.o")]
         links.append((name, link + ["-o", str(targets[name])] + objs +
                       (engine if with_engine else []) + host))
-    for name in BENCHES:
-        links.append((name, link + ["-o", str(targets[name]), str(obj / f"{name}.o")] + engine +
-                      host))
+    for name, (_, with_engine) in BENCHES.items():
+        links.append((name, link + ["-o", str(targets[name]), str(obj / f"{name}.o")] +
+                      (engine if with_engine else []) + host))
     for name in SYNTHETIC_TESTS:
         srcs, with_engine = TESTS[name]
         objs = [str(obj / "synthetic" / f"{Path(s).stem}.o") for s in srcs] + \
