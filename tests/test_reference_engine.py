@@ -73,3 +73,17 @@ def test_synthetic_model_matches_the_reference_models_tensor_manifest(tmp_path):
         assert (ty, dims) == (wt, wd), name
     g = gguf.GGUFReader(str(tmp_path / "g" / "ornith-layers.gguf"))
     assert "golden.token_ids" in g.fields and "golden.continuation_ids" in g.fields
+
+
+@pytest.mark.parametrize("kind,k", [("q4k", 2048), ("q4k", 4096), ("q6k", 512), ("q6k", 2048)])
+def test_synthetic_weights_have_unit_variance_projections(kind, k):
+    """The synthetic model's weights: standard deviation ~ 1 / sqrt(k) and mean ~ 0, so each
+    projection maps unit-variance inputs to roughly unit-variance outputs."""
+    import numpy as np
+    from oracle import quant as Q
+    from support import synthetic_model as S
+    rng = np.random.RandomState(k)
+    raw = S._q4k(rng, 64, k) if kind == "q4k" else S._q6k(rng, 64, k)
+    w = (Q.q4k_dequant(raw) if kind == "q4k" else Q.q6k_dequant(raw)).astype(np.float64)
+    assert 0.7 < w.std() * np.sqrt(k) < 1.4
+    assert abs(w.mean()) < 0.1 * w.std()
