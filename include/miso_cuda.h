@@ -237,9 +237,12 @@ int miso_deltanet_chunk(const miso_deltanet_chunk_params* p, void* stream);
  *   core[b][h][d] = softmax(q[b][h] . K^T / 16) V [d] * sigmoid(qg[b * qg_stride + h*512 + 256 + d])
  * lens[b] == 0 gives core = 0. Work is divided evenly over the SMs by key tiles (stream-K); a
  * sequence cut across CTAs is merged by the last CTA to finish it, using `scratch`.
- * scratch: at least miso_attn_decode_scratch_bytes(batch) bytes, ZEROED BEFORE ITS FIRST USE;
- * every successful call leaves it ready for the next one (calls sharing one scratch buffer must
- * not overlap in time). Requires batch <= 1024, pool_rows < 2^31, 16-byte aligned pools. */
+ * scratch: at least miso_attn_decode_scratch_bytes(batch) bytes, 256-byte aligned, any contents:
+ * every call first zeroes the 2 * batch arrival counters at its start (an 8-byte-per-sequence
+ * memset on `stream`, before the kernel), so the leftovers of an earlier call - including one
+ * whose kernel gave up on a bounded wait and left counters set (miso_device_status then reports
+ * MISO_STATUS_TIMEOUT) - do not reach the next call. Calls sharing one scratch buffer must not
+ * overlap in time. Requires batch <= 1024, pool_rows < 2^31, 16-byte aligned pools. */
 typedef struct {
   const float* q;         /* [batch][16][256] normalised, rotated queries (unscaled) */
   const float* qg;        /* gate of (b, h, d) at qg[b * qg_stride + h * 512 + 256 + d] */
@@ -262,8 +265,9 @@ int miso_attn_decode(const miso_attn_decode_params* p, void* scratch, size_t scr
  * results as miso_attn_decode, without the scratch argument: the scratch is a fixed array inside
  * the library (2,643,968 bytes, present on every GPU that loads the library until exit). Limits:
  * batch <= 256 (MISO_ERR_LIMIT beyond). Allocates nothing. The first call on each device looks up
- * the array's address and should come before any stream capture. All calls on a device share the
- * array: calls that overlap on the GPU race. */
+ * the array's address and should come before any stream capture (a failed lookup is returned as
+ * that call's error and retried by the next call). All calls on a device share the array: calls
+ * that overlap on the GPU race. */
 int miso_attn_decode_noalloc(const miso_attn_decode_params* p, void* stream);
 
 /* Batched decode prep: attn_prep_kernel (kernels/attention_decode.hpp:41-83) for `batch`

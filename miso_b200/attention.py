@@ -153,7 +153,7 @@ class KvPool:
 
 
 def decode_scratch(batch: int, device="cuda") -> torch.Tensor:
-    """Scratch for decode_batched, zeroed (the library keeps it zeroed between calls)."""
+    """Scratch for decode_batched (any contents: each call zeroes the counters it uses)."""
     n = int(capi.load().miso_attn_decode_scratch_bytes(batch))
     if n == 0:
         raise capi.MisoError("miso_attn_decode_scratch_bytes", -3)

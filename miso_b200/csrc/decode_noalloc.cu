@@ -19,7 +19,8 @@
 //
 // Host code cannot use the array's name as a device address (there it names a host-side stand-in).
 // The first call on each device, with that device current, looks the address up with
-// cudaGetSymbolAddress and remembers it; make that first call before any stream capture.
+// cudaGetSymbolAddress and remembers it; make that first call before any stream capture. A
+// lookup that fails is not remembered: that call returns the error and the next call retries.
 //
 // This file is part of the single translation unit of capi.cu (included at its end), next to the
 // kernel and the helpers it reuses.
@@ -39,15 +40,13 @@ static __device__ __align__(256) unsigned char g_decode_noalloc_scratch[kNoAlloc
 
 namespace {
 
-struct NoAllocDevice {
-  std::once_flag once;
-  int status = MISO_OK;
-  void* scratch = nullptr;  // device address of g_decode_noalloc_scratch on this device
-};
+// Device address of g_decode_noalloc_scratch on each device; null until a lookup succeeded.
+void* g_noalloc_scratch[kMaxDevices] = {};
+std::mutex g_noalloc_mutex;
 
-NoAllocDevice g_noalloc[kMaxDevices];
-
-// Device address of the scratch array on the current device (looked up once per device).
+// Device address of the scratch array on the current device. Only a successful lookup is kept:
+// a failed one (for example, a first call made during stream capture) returns its error and the
+// next call looks again.
 int noalloc_scratch(void** out) {
   int dev = 0;
   const cudaError_t e = cudaGetDevice(&dev);
@@ -55,18 +54,18 @@ int noalloc_scratch(void** out) {
     return static_cast<int>(e);
   if (dev < 0 || dev >= kMaxDevices)
     return MISO_ERR_NO_DEVICE;
-  NoAllocDevice& d = g_noalloc[dev];
-  std::call_once(d.once, [&] {
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_scratch[dev] == nullptr) {
     void* p = nullptr;
     const cudaError_t r = cudaGetSymbolAddress(&p, g_decode_noalloc_scratch);
-    if (r != cudaSuccess || p == nullptr) {
-      d.status = r != cudaSuccess ? static_cast<int>(r) : MISO_ERR_NO_DEVICE;
-      return;
-    }
-    d.scratch = p;
-  });
-  *out = d.scratch;
-  return d.status;
+    if (r != cudaSuccess)
+      return static_cast<int>(r);
+    if (p == nullptr)
+      return MISO_ERR_NO_DEVICE;
+    g_noalloc_scratch[dev] = p;
+  }
+  *out = g_noalloc_scratch[dev];
+  return MISO_OK;
 }
 
 }  // namespace

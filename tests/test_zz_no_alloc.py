@@ -10,6 +10,11 @@ decode tests' tolerance (relative L2 <= 1e-5 per head). It does this on two call
 the second call meets the first call's leftovers in the shared array. It also checks that a batch
 beyond the fixed limit is refused with MISO_ERR_LIMIT.
 
+Only calls that succeed are covered. Each call also zeroes the shared counters before its kernel,
+which matters after a call whose kernel gave up on a bounded wait; no call here is made to give
+up, so that zeroing is not exercised (a successful call leaves the counters at zero anyway). The
+same zeroing in miso_attn_decode is tested with planted leftovers in test_gpu_attention.py.
+
 The file name sorts last so that a run stopping at the first failure has already run every other
 test.
 """
