@@ -164,6 +164,27 @@ def deltanet_seq(n: int, qkv, qkv_stride: int, zab, zab_stride: int, conv_w, con
     return out
 
 
+def deltanet_seq_heads(n: int, qkv, qkv_stride: int, zab, zab_stride: int, conv_w, conv, ssm_a,
+                       dt_bias, norm_w, state, eps: float, heads, z_off: int = 0,
+                       a_off: int = 4096, b_off: int = 4128, threads: int = 0):
+    """deltanet_seq for the listed V heads only: state ([32][128][128] float64) updated in place
+    for those heads; returns out [n][len(heads)][128] (the heads' outputs in list order). The conv
+    history `conv` (float64 [8192][3]) is read, not updated."""
+    qkv = _f32(qkv); zab = _f32(zab)
+    hs = np.ascontiguousarray(heads, dtype=np.uint32)
+    conv = np.ascontiguousarray(conv, dtype=np.float64)
+    assert state.dtype == np.float64 and state.flags["C_CONTIGUOUS"]
+    out = np.zeros((n, hs.shape[0], 128))
+    w = [_f32(x) for x in (conv_w, ssm_a, dt_bias, norm_w)]
+    base = zab.ctypes.data
+    z, a, b = (C.c_void_p(base + 4 * off) for off in (z_off, a_off, b_off))
+    _load().oracle_deltanet_seq_heads(C.c_uint(n), _p(qkv), C.c_uint(qkv_stride), z, a, b,
+                                      C.c_uint(zab_stride), _p(w[0]), _p(conv), _p(w[1]),
+                                      _p(w[2]), _p(w[3]), _p(state), _p(out), C.c_float(eps),
+                                      _p(hs), C.c_uint(hs.shape[0]), C.c_int(threads))
+    return out
+
+
 def deltanet_prepare(n: int, qkv, a, b, conv_w, conv, ssm_a, dt_bias):
     """Conv + SiLU + norms of the chunked form: returns q, k, v, beta, log_a (float64)."""
     qkv = _f32(qkv); a = _f32(a); b = _f32(b)

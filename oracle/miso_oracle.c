@@ -33,6 +33,21 @@ double oracle_half_to_double(uint16_t h) {
   return sign ? -v : v;
 }
 
+/* Every binary16 value as a double, built once (exact: the same values as
+ * oracle_half_to_double), so the attention loops index a table instead of decoding each element. */
+static double g_half[65536];
+static pthread_once_t g_half_once = PTHREAD_ONCE_INIT;
+
+static void half_table_init(void) {
+  for (unsigned h = 0; h < 65536; ++h)
+    g_half[h] = oracle_half_to_double((uint16_t)h);
+}
+
+static const double* half_table(void) {
+  pthread_once(&g_half_once, half_table_init);
+  return g_half;
+}
+
 int oracle_cpu_count(void) {
   const long n = sysconf(_SC_NPROCESSORS_ONLN);
   return n > 0 ? (int)n : 1;
@@ -150,12 +165,13 @@ static void attend_row(const float* q, const float* gate, const uint16_t* K, con
       out[e] = 0.0;
     return;
   }
+  const double* H = half_table();
   double mx = -INFINITY;
   for (unsigned j = 0; j < len; ++j) {
     double dot = 0.0;
     const uint16_t* kr = K + (size_t)j * D;
     for (int e = 0; e < D; ++e)
-      dot += (double)q[e] * oracle_half_to_double(kr[e]);
+      dot += (double)q[e] * H[kr[e]];
     s[j] = dot / 16.0;
     if (s[j] > mx)
       mx = s[j];
@@ -170,7 +186,7 @@ static void attend_row(const float* q, const float* gate, const uint16_t* K, con
   for (unsigned j = 0; j < len; ++j) {
     const uint16_t* vr = V + (size_t)j * D;
     for (int e = 0; e < D; ++e)
-      out[e] += s[j] * oracle_half_to_double(vr[e]);
+      out[e] += s[j] * H[vr[e]];
   }
   for (int e = 0; e < D; ++e)
     out[e] = out[e] / l / (1.0 + exp(-(double)gate[e]));
@@ -381,12 +397,14 @@ typedef struct {
   double* state;
   double* out;
   float eps;
+  const unsigned* heads; /* V heads to run (NULL: all DN_VH, item = head) */
+  unsigned n_heads;      /* with heads: out is [n][n_heads][128] in list order */
 } seq_ctx;
 
 /* One V head over all n tokens; each head keeps private copies of its channels' histories. */
 static void seq_head_item(void* vctx, size_t hh) {
   const seq_ctx* c = (const seq_ctx*)vctx;
-  const int h = (int)hh, kh = h % DN_KH;
+  const int h = c->heads ? (int)c->heads[hh] : (int)hh, kh = h % DN_KH;
   double* hist = (double*)malloc(sizeof(double) * 3 * DN_D * 3);
   const int chq = kh * DN_D, chk = DN_KH * DN_D + kh * DN_D, chv = 2 * DN_KH * DN_D + h * DN_D;
   for (int i = 0; i < DN_D; ++i)
@@ -411,8 +429,10 @@ static void seq_head_item(void* vctx, size_t hh) {
     const size_t zr = (size_t)t * c->zab_stride;
     const double beta = sigmoid(c->b[zr + h]);
     const double decay = exp(c->ssm_a[h] * softplus((double)c->a[zr + h] + c->dt_bias[h]));
+    double* o = c->heads ? c->out + ((size_t)t * c->n_heads + hh) * DN_D
+                         : c->out + (size_t)t * DN_OUT + h * DN_D;
     delta_rule(c->state + (size_t)h * DN_D * DN_D, q, k, v, beta, decay, c->norm_w,
-               c->z + zr + h * DN_D, c->eps, c->out + (size_t)t * DN_OUT + h * DN_D);
+               c->z + zr + h * DN_D, c->eps, o);
   }
   free(hist);
 }
@@ -423,8 +443,8 @@ void oracle_deltanet_seq(unsigned n, const float* qkv, unsigned qkv_stride, cons
                          const float* norm_w, double* state, double* out, float eps, int threads) {
   double* conv0 = (double*)malloc(sizeof(double) * DN_CH * 3);
   memcpy(conv0, conv, sizeof(double) * DN_CH * 3);
-  seq_ctx c = {n,      qkv,     qkv_stride, z,     a,   b,  zab_stride, conv_w, conv0,
-               ssm_a,  dt_bias, norm_w,     state, out, eps};
+  seq_ctx c = {n,     qkv,     qkv_stride, z,     a,   b,   zab_stride, conv_w, conv0,
+               ssm_a, dt_bias, norm_w,     state, out, eps, NULL, 0};
   parallel_for(DN_VH, threads, seq_head_item, &c);
   /* Final history: the last three inputs of each channel (older history if n < 3). */
   for (int ch = 0; ch < DN_CH; ++ch) {
@@ -433,6 +453,21 @@ void oracle_deltanet_seq(unsigned n, const float* qkv, unsigned qkv_stride, cons
       shift_hist(hist, qkv[(size_t)t * qkv_stride + ch]);
   }
   free(conv0);
+}
+
+/* oracle_deltanet_seq for the listed V heads only (each head is independent of the others):
+ * their state slices [h] are updated and their outputs written to out [n][n_heads][128] in list
+ * order. The conv history is read, not updated. Same restatement as above
+ * (kernels/deltanet_step.hpp:146-273). */
+void oracle_deltanet_seq_heads(unsigned n, const float* qkv, unsigned qkv_stride, const float* z,
+                               const float* a, const float* b, unsigned zab_stride,
+                               const float* conv_w, const double* conv, const float* ssm_a,
+                               const float* dt_bias, const float* norm_w, double* state,
+                               double* out, float eps, const unsigned* heads, unsigned n_heads,
+                               int threads) {
+  seq_ctx c = {n,     qkv,     qkv_stride, z,     a,   b,   zab_stride, conv_w, conv,
+               ssm_a, dt_bias, norm_w,     state, out, eps, heads, n_heads};
+  parallel_for(n_heads, threads, seq_head_item, &c);
 }
 
 /* kernels/deltanet_chunk.hpp:41-112 */

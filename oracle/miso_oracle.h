@@ -73,6 +73,16 @@ void oracle_deltanet_seq(unsigned n, const float* qkv, unsigned qkv_stride, cons
                          double* conv, const float* ssm_a, const float* dt_bias,
                          const float* norm_w, double* state, double* out, float eps, int threads);
 
+/* oracle_deltanet_seq restricted to the n_heads V heads listed in `heads` (the heads do not
+ * interact): updates their state slices and writes their outputs to out [n][n_heads][128] (list
+ * order); the conv history is read, not updated. */
+void oracle_deltanet_seq_heads(unsigned n, const float* qkv, unsigned qkv_stride, const float* z,
+                               const float* a, const float* b, unsigned zab_stride,
+                               const float* conv_w, const double* conv, const float* ssm_a,
+                               const float* dt_bias, const float* norm_w, double* state,
+                               double* out, float eps, const unsigned* heads, unsigned n_heads,
+                               int threads);
+
 /* Conv + SiLU + norm pass of the chunked form (kernels/deltanet_chunk.hpp:41-112): from qkv
  * [n][8192], a / b [n][32] produce q, k [n][16][128] (L2-normalised, q also / sqrt(128)),
  * v [n][32][128], beta and log_a [n][32]; conv history updated in place. */

@@ -169,3 +169,25 @@ def test_deltanet_state_is_affine_in_the_incoming_state():
     a = run(x_nov, conv_nov, np.broadcast_to(np.eye(128), (32, 128, 128)).copy())
     pred = np.einsum("hkm,hmv->hkv", a, s_in) + s_zero
     assert np.abs(pred - s_full).max() <= 1e-12 * max(1.0, np.abs(s_full).max())
+
+
+def test_head_subset_recurrence_equals_the_full_one():
+    """oracle.deltanet_seq_heads (used to check long sequences on a few heads) gives exactly the
+    full recurrence's state slices and output columns of the listed heads."""
+    rng = np.random.RandomState(21)
+    n = 37
+    qkv = rng.standard_normal((n, 8192)).astype(np.float32)
+    zab = rng.standard_normal((n, 4160)).astype(np.float32)
+    cw = (0.5 * rng.standard_normal((8192, 4))).astype(np.float32)
+    conv = rng.standard_normal((8192, 3))
+    sa, dt = -np.ones(32, np.float32), np.zeros(32, np.float32)
+    nw = np.ones(128, np.float32)
+    s_full = 0.1 * rng.standard_normal((32, 128, 128))
+    s_sub = s_full.copy()
+    out = oracle.deltanet_seq(n, qkv, 8192, zab, 4160, cw, conv.copy(), sa, dt, nw, s_full, 1e-6)
+    heads = [1, 16, 31]
+    sub = oracle.deltanet_seq_heads(n, qkv, 8192, zab, 4160, cw, conv, sa, dt, nw, s_sub, 1e-6,
+                                    heads)
+    for i, h in enumerate(heads):
+        assert np.array_equal(s_sub[h], s_full[h])
+        assert np.array_equal(sub[:, i], out[:, h * 128:(h + 1) * 128])
