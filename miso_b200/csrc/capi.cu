@@ -390,8 +390,14 @@ int miso_attn_decode(const miso_attn_decode_params* p, void* scratch, size_t scr
   a.parts = reinterpret_cast<float*>(static_cast<char*>(scratch) + decode_counter_bytes(p->batch));
   a.batch = p->batch;
   a.qg_stride = p->qg_stride;
-  dec::decode_kernel<<<d->sms, dec::kThreads, dec::kSmemBytes, as_stream(stream)>>>(kmap, vmap,
-                                                                                    a);
+  // The kernel returns every counter to zero, but a call whose bounded waits gave up does not:
+  // start each call from zeroed counters so such a call cannot corrupt the next one.
+  const cudaError_t e = cudaMemsetAsync(scratch, 0, size_t(2) * p->batch * sizeof(int),
+                                        as_stream(stream));
+  if (e != cudaSuccess)
+    return static_cast<int>(e);
+  const unsigned ctas = d->sms < int(dec::kMaxCtas) ? unsigned(d->sms) : dec::kMaxCtas;
+  dec::decode_kernel<<<ctas, dec::kThreads, dec::kSmemBytes, as_stream(stream)>>>(kmap, vmap, a);
   return launch_status();
 }
 

@@ -45,9 +45,13 @@ constexpr int kBoxBytes = 64 * 128;            // TMA box: 64 rows x 64 dims fp1
 constexpr int kHalfStage = 4 * kBoxBytes;      // K (or V) of one tile
 constexpr int kStageBytes = 2 * kHalfStage;    // 64 KiB
 constexpr int kMaxBatch = 1024;
+constexpr unsigned kMinTiles = 2;              // fewest tiles a working CTA takes
+constexpr unsigned kMaxCtas = 256;             // grid limit: the merge weights fit one slot
 constexpr int kSlotRow = 260;                  // padded [head][dim] row of a merge slot (floats)
 constexpr int kSlotFloats = kGroup * kSlotRow + kGroup;  // o[8][260] then l[8]
 constexpr int kPartFloats = 2 * kGroup + kGroup * kDim;  // m[8], l[8], o[8][256]
+static_assert(kMaxCtas * kGroup + kGroup <= kSlotFloats, "merge weights [P][8] + L[8] in a slot");
+static_assert(kMaxCtas <= kSlotFloats, "merge offsets [P] in the other slot");
 
 struct Args {
   const float* q;
@@ -109,7 +113,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* stages = base;
   Smem& sm = *reinterpret_cast<Smem*>(base + size_t(kStages) * kStageBytes);
   const unsigned tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
-  const unsigned P = gridDim.x, c = blockIdx.x;
+  const unsigned c = blockIdx.x;
   const float kNegInf = -__int_as_float(0x7f800000);
 
   // ---- tile prefix over sequences: seq_start[b] = sum_{b' < b} 2 ceil(len / 64) ----------------
@@ -148,8 +152,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
 
   const unsigned T = static_cast<unsigned>(sm.seq_start[a.batch]);
-  const unsigned t_begin = T == 0 ? 0 : range_begin(c, T, P);
-  const unsigned t_end = T == 0 ? 0 : range_begin(c + 1, T, P);
+  // At least kMinTiles tiles per working CTA: with fewer, half of the consumer warps idle and a
+  // segment is cut into more partials than its bytes justify (small batches, short contexts).
+  // CTAs c >= P get an empty range.
+  const unsigned P = max(1u, min(gridDim.x, T / kMinTiles));
+  const unsigned t_begin = (T == 0 || c >= P) ? T : range_begin(c, T, P);
+  const unsigned t_end = (T == 0 || c >= P) ? T : range_begin(c + 1, T, P);
 
   // ---------------------------------------------------------------------------------- producer
   if (warp == kConsumerWarps) {
@@ -330,28 +338,60 @@ __global__ void __launch_bounds__(kThreads, 1)
         __threadfence();
         const unsigned seg_at_cfirst_start =
             static_cast<unsigned>(range_begin(c_first, T, P)) >= seg_first;
-        for (unsigned i = tid; i < kGroup * kDim; i += kConsumers) {
-          const unsigned h = i / kDim, d = i % kDim;
+        // The segment's partials, in CTA order: CTA c_first + k wrote slot sl(k) (its second
+        // slot when the segment is not the first of its range), or nothing for an empty range.
+        const unsigned np = c_last - c_first + 1;
+        // Partial k's slot index (or -1 for an empty range), computed once: the range bounds
+        // take 64-bit divisions. The slots are free: this CTA's own result is in its partial.
+        int* poff = reinterpret_cast<int*>(sm.slot[1]);  // [np]
+        for (unsigned k = tid; k < np; k += kConsumers) {
+          const unsigned cc = c_first + k;
+          const unsigned sl = (cc > c_first || seg_at_cfirst_start) ? 0 : 1;
+          poff[k] = range_begin(cc, T, P) == range_begin(cc + 1, T, P) ? -1 : int(2 * cc + sl);
+        }
+        dev::named_bar_sync(1, kConsumers);
+        auto part_of = [&](unsigned k) -> const float* {
+          const int o = poff[k];
+          return o < 0 ? nullptr : a.parts + size_t(o) * kPartFloats;
+        };
+        // Weights: warp h finds head h's max over the partials, then w[k][h] = e^(m_k - M) and,
+        // in lane 0, in partial order, L[h] = sum_k w[k][h] l_k.
+        float* wts = sm.slot[0];             // [np][kGroup]
+        float* Ls = sm.slot[0] + np * kGroup;  // [kGroup]
+        {
+          const unsigned h = warp;
           float M = kNegInf;
-          for (unsigned cc = c_first; cc <= c_last; ++cc) {
-            if (range_begin(cc, T, P) == range_begin(cc + 1, T, P))
-              continue;  // empty range: no partial
-            const unsigned sl = (cc > c_first || seg_at_cfirst_start) ? 0 : 1;
-            const float* pp = a.parts + (size_t(2) * cc + sl) * kPartFloats;
-            M = fmaxf(M, __ldcg(pp + h));
+          for (unsigned k = lane; k < np; k += 32)
+            if (const float* pp = part_of(k))
+              M = fmaxf(M, __ldcg(pp + h));
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1)
+            M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+          for (unsigned k = lane; k < np; k += 32) {
+            const float* pp = part_of(k);
+            const float mc = pp ? __ldcg(pp + h) : kNegInf;
+            wts[k * kGroup + h] = mc == kNegInf ? 0.0f : fast_exp(mc - M);
           }
-          float L = 0.0f, ov = 0.0f;
-          for (unsigned cc = c_first; cc <= c_last; ++cc) {
-            if (range_begin(cc, T, P) == range_begin(cc + 1, T, P))
-              continue;
-            const unsigned sl = (cc > c_first || seg_at_cfirst_start) ? 0 : 1;
-            const float* pp = a.parts + (size_t(2) * cc + sl) * kPartFloats;
-            const float mc = __ldcg(pp + h);
-            const float w = mc == kNegInf ? 0.0f : fast_exp(mc - M);
-            L += w * __ldcg(pp + kGroup + h);
-            ov += w * __ldcg(pp + 2 * kGroup + i);
+          __syncwarp();
+          if (lane == 0) {
+            float L = 0.0f;
+            for (unsigned k = 0; k < np; ++k)
+              if (const float* pp = part_of(k))
+                L += wts[k * kGroup + h] * __ldcg(pp + kGroup + h);
+            Ls[h] = L;
           }
-          out[h * kDim + d] = ov / L / (1.0f + fast_exp(-gate[h * 2 * kDim + d]));
+        }
+        dev::named_bar_sync(1, kConsumers);
+        // Outputs: thread tid takes dimension tid of every head; the loads of different partials
+        // are independent, so several are in flight at once.
+        for (unsigned h = 0; h < kGroup; ++h) {
+          const unsigned i = h * kDim + tid;
+          float ov = 0.0f;
+#pragma unroll 4
+          for (unsigned k = 0; k < np; ++k)
+            if (const float* pp = part_of(k))
+              ov += wts[k * kGroup + h] * __ldcg(pp + 2 * kGroup + i);
+          out[i] = ov / Ls[h] / (1.0f + fast_exp(-gate[h * 2 * kDim + tid]));
         }
         if (tid == 0)
           a.counters[seg] = 0;  // ready for the next call

@@ -202,6 +202,25 @@ def test_fast_decode_ragged_batch_with_empty_sequences():
     check_status()
 
 
+def test_fast_decode_ignores_leftover_counters_in_scratch():
+    """A call whose kernel gave up on a bounded wait leaves arrival counters set. Each call zeroes
+    its counters before its kernel, so a scratch buffer holding such leftovers (planted here from
+    the host: every counter and partial set to garbage) still gives the oracle's result."""
+    lens = [3000, 1, 777, 0, 2049, 64, 5000]
+    pool, k, v, q, qg = make_pool(lens, 5120, seed=8)
+    scratch = A.decode_scratch(pool.batch, device=DEV)
+    scratch.fill_(0x3F00_0001)  # counters at ~1e9 arrivals, partials at 0.5-ish floats
+    got, _ = run_fast(pool, q, qg, scratch)
+    ref = oracle_pool(pool, k, v, q, qg, lens)
+    live = [b for b, n in enumerate(lens) if n > 0]
+    assert rel_per_head(got[live], ref[live]) <= 1e-5
+    assert np.all(got[3] == 0.0)
+    scratch[: 2 * len(lens)].fill_(-7)  # negative counts too
+    again, _ = run_fast(pool, q, qg, scratch)
+    assert np.array_equal(again.view(np.uint32), got.view(np.uint32))
+    check_status()
+
+
 def test_fast_decode_long_ragged_batch():
     rng = np.random.RandomState(0)
     lens = list(rng.randint(1024, 20000, size=8))
