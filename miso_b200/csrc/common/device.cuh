@@ -1,7 +1,7 @@
 #pragma once
 
 // sm_100a device building blocks shared by the fast kernels: shared-memory addressing, mbarriers
-// with bounded waits, TMA tile loads, ldmatrix / movmatrix and the m16n8k16 f16 MMA.
+// with bounded waits, TMA tile loads (the warp-level MMA fragments are in warp_mma.cuh).
 //
 // Every wait on an mbarrier is bounded (SM clock cycles). When a wait gives up, the kernel records
 // MISO_STATUS_TIMEOUT and the waiting site in the library's device status word and stops issuing
@@ -12,6 +12,8 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+
+#include "warp_mma.cuh"
 
 namespace miso::dev {
 
@@ -147,58 +149,6 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
 // CU_TENSOR_MAP_SWIZZLE_128B and 128-byte rows (box base aligned to 1024 bytes).
 __device__ __forceinline__ uint32_t swz128(uint32_t row, uint32_t chunk) {
   return row * 128u + (((chunk ^ row) & 7u) << 4);
-}
-
-// ---- warp-level tensor-core fragments -------------------------------------------------------
-
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
-                                        uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr)
-               : "memory");
-}
-
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
-                                          uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr)
-               : "memory");
-}
-
-// Transpose of an 8x8 b16 matrix held in the standard fragment layout (lane i: row i/4,
-// columns 2(i%4), 2(i%4)+1).
-__device__ __forceinline__ uint32_t movmatrix_t(uint32_t a) {
-  uint32_t d;
-  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
-  return d;
-}
-
-// D = A(16x16, row) * B(16x8, col) + D, f16 inputs, f32 accumulate.
-__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
-                                        uint32_t a3, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
-      "{%8, %9}, {%0, %1, %2, %3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ uint32_t pack_half2(float lo_elem, float hi_elem) {
-  const __half2 h = __floats2half2_rn(lo_elem, hi_elem);
-  return *reinterpret_cast<const uint32_t*>(&h);
-}
-
-// Two-term fp16 split of an fp32 pair: hi = fp16(x), lo = fp16(x - hi). hi + lo carries ~22
-// significant bits, so products against exact fp16 operands keep fp32-level accuracy.
-__device__ __forceinline__ void split_half2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
-  const __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
-  const __half l0 = __float2half_rn(x0 - __half2float(h0));
-  const __half l1 = __float2half_rn(x1 - __half2float(h1));
-  const __half2 H = __halves2half2(h0, h1), L = __halves2half2(l0, l1);
-  hi = *reinterpret_cast<const uint32_t*>(&H);
-  lo = *reinterpret_cast<const uint32_t*>(&L);
 }
 
 __device__ __forceinline__ void named_bar_sync(unsigned id, unsigned threads) {

@@ -17,6 +17,7 @@
 #include <cstddef>
 #include <cstdint>
 
+#include "../common/warp_mma.cuh"
 #include "wave.hpp"
 
 namespace miso::kernels {
@@ -221,89 +222,262 @@ struct AttnSplitParams {
   unsigned len, max_ctx, n_splits;
 };
 
+namespace attn_detail {
+
+// Merge slot of the split kernel: [8 heads][256 dims] fp32 then l[8]. Dims are stored in rows of
+// 33 per group of 32 and heads 268 floats apart, so the stores of a fragment (lane (g, tq):
+// heads 2 tq, 2 tq + 1, dims 32 g + ...) fall in 32 different banks.
+constexpr int kSplitSlotHead = 268;
+constexpr int kSplitSlotFloats = 8 * kSplitSlotHead + 8;
+__device__ __forceinline__ int split_slot_index(unsigned h, unsigned d) {
+  return int(h) * kSplitSlotHead + int(d / 32) * 33 + int(d % 32);
+}
+
+}  // namespace attn_detail
+
 // Items [first, first + count) with item = kvh * n_splits + split. Split `split` covers the
-// positions [split * per * 32, min(len, (split + 1) * per * 32)) with per = ceil(subs / n_splits).
-// One warp per query head of the KV group: in the score phase lane j owns key j of a 32-key
-// sub-chunk (K staged in padded shared rows, conflict-free); in the value phase lane i owns
-// dims [8i, 8i + 8) and the probabilities are broadcast by shuffle. The online softmax state
-// (max, sum) is warp-uniform and lives in registers.
+// positions [split * per * 32, min(len, (split + 1) * per * 32)) with per = ceil(subs / n_splits)
+// (the reference partition; the combine merges the splits' (max, sum, output) triples).
+//
+// Tensor-core body inside the caller's geometry (kBlock = 256 threads = 8 warps, no dynamic shared
+// memory). The split's keys are cut into 16-key slabs; warp w takes slabs w, w + 8, ... and
+// streams each slab straight from global memory into mma.sync m16n8k16 fragments (no shared-
+// memory staging, so each warp has a whole slab of K and V - 16 KB - in flight, and the next
+// slab's loads are issued while the current one is computed):
+//   S^T[16 keys][8 heads] = K Q^T      with the head dimension permuted so that a lane's K
+//                                      fragment elements are its 64 contiguous dims
+//                                      [64 tq, 64 tq + 64) of keys g and g + 8 (eight 16-byte
+//                                      loads per key); Q uses the same permutation
+//   O^T[256 dims][8 heads] += V^T P^T  with the output dims permuted so that a lane reads dims
+//                                      [32 g, 32 g + 32) of keys 2 tq, 2 tq + 1, 2 tq + 8,
+//                                      2 tq + 9, and pairs the two keys' halves by byte permutes
+// (g = lane / 4, tq = lane % 4). The fp32 query and the probabilities are split into fp16 high and
+// low parts (two MMAs each; K and V are exact fp16), so the result keeps fp32 accuracy; the online
+// softmax is per warp, and the eight warp states are merged through shared memory at the end.
 template <int kBlock>
 __device__ void attn_split_op(const AttnSplitParams& p, unsigned first, unsigned count) {
   using namespace attn;
-  constexpr int kGroup = kQHeads / kKvHeads, kSub = kAttnSubChunk;
-  constexpr int kKRow = kDim / 2 + 1;  // half2 per padded K row: 129 words
-  static_assert(kBlock == kGroup * kWave, "one warp per query head of the KV group");
-  static_assert(kSub == kWave, "one lane per key of a sub-chunk");
-  __shared__ float qs[kGroup][kDim];
-  __shared__ __half2 ks[kSub][kKRow];
-  __shared__ __align__(16) uint4 vs[kSub][kDim / 8];
-  const unsigned tid = threadIdx.x, lane = tid % kWave, h = tid / kWave;
-  const float scale = rsqrtf(static_cast<float>(kDim));
-  const unsigned subs = (p.len + kSub - 1) / kSub;
+  using attn_detail::kSplitSlotFloats;
+  using attn_detail::split_slot_index;
+  constexpr int kGroup = kQHeads / kKvHeads, kSlab = 16, kWarps = kBlock / kWave;
+  static_assert(kBlock == kGroup * kWave && kWave == 32, "eight 32-lane warps");
+  __shared__ uint4 qfrag[16][32];  // per k-step and lane: Q^T fragments {hi b0, hi b1, lo b0, lo b1}
+  __shared__ float slot[2][kSplitSlotFloats];
+  __shared__ float red_m[kWarps][kGroup];
+  const unsigned tid = threadIdx.x, warp = tid / kWave, lane = tid % kWave;
+  const unsigned g = lane / 4, tq = lane % 4;
+  const float kNegInf = -__int_as_float(0x7f800000);
+  const unsigned subs = (p.len + kAttnSubChunk - 1) / kAttnSubChunk;
   const unsigned per = (subs + p.n_splits - 1) / p.n_splits;
+  const uint64_t policy = dev::stream_policy();
 
   for (unsigned item = first + blockIdx.y * gridDim.x + blockIdx.x; item < first + count;
        item += gridDim.x * gridDim.y) {
     const unsigned kvh = item / p.n_splits, split = item % p.n_splits;
-    const __half2* K = reinterpret_cast<const __half2*>(p.k_cache + std::size_t{kvh} * p.max_ctx * kDim);
-    const uint4* V = reinterpret_cast<const uint4*>(p.v_cache + std::size_t{kvh} * p.max_ctx * kDim);
-    for (unsigned i = tid; i < kGroup * kDim; i += kBlock)
-      qs[i / kDim][i % kDim] = p.q[kvh * kGroup * kDim + i] * scale;
-    float m = -__int_as_float(0x7f800000), l = 0.0f, acc[8] = {};
-    const unsigned j_begin = split * per * kSub;
-    const unsigned j_end = min(p.len, (split + 1) * per * kSub);
+    const half_t* K = p.k_cache + std::size_t{kvh} * p.max_ctx * kDim;
+    const half_t* V = p.v_cache + std::size_t{kvh} * p.max_ctx * kDim;
+    const unsigned j_begin = split * per * kAttnSubChunk;
+    const unsigned j_end = min(p.len, (split + 1) * per * kAttnSubChunk);
+    const unsigned nslab = j_end > j_begin ? (j_end - j_begin + kSlab - 1) / kSlab : 0;
+
+    // Q^T fragments of the group's 8 heads (pre-scaled by 1/16, exact): k-step ks, lane (fg, ft)
+    // holds dims 64 ft + 4 ks + {0, 1} (b0) and + {2, 3} (b1) of head fg, as fp16 hi and lo.
+    for (unsigned e = tid; e < 16 * 32; e += kBlock) {
+      const unsigned ks = e / 32, ln = e % 32, fg = ln / 4, ft = ln % 4;
+      const float4 x = *reinterpret_cast<const float4*>(p.q + (kvh * kGroup + fg) * kDim +
+                                                        64 * ft + 4 * ks);
+      uint4 f;
+      dev::split_half2(x.x * 0.0625f, x.y * 0.0625f, f.x, f.z);
+      dev::split_half2(x.z * 0.0625f, x.w * 0.0625f, f.y, f.w);
+      qfrag[ks][ln] = f;
+    }
     __syncthreads();
 
-    for (unsigned j0 = j_begin; j0 < j_end; j0 += kSub) {
-      const unsigned n = min(static_cast<unsigned>(kSub), j_end - j0);
-      for (unsigned e = tid; e < kSub * (kDim / 2); e += kBlock) {
-        const unsigned r = e / (kDim / 2), c = e % (kDim / 2);
-        if (r < n)
-          ks[r][c] = K[std::size_t{j0 + r} * (kDim / 2) + c];
-      }
-      for (unsigned e = tid; e < kSub * (kDim / 8); e += kBlock) {
-        const unsigned r = e / (kDim / 8), c = e % (kDim / 8);
-        if (r < n)
-          vs[r][c] = V[std::size_t{j0 + r} * (kDim / 8) + c];
-      }
-      __syncthreads();
-      float s = -__int_as_float(0x7f800000);
-      if (lane < n) {
-        s = 0.0f;
-#pragma unroll 8
-        for (int e = 0; e < kDim / 2; ++e) {
-          const float2 kf = __half22float2(ks[lane][e]);
-          s += qs[h][2 * e] * kf.x + qs[h][2 * e + 1] * kf.y;
-        }
-      }
-      const float m_new = fmaxf(m, wave_max(s));
-      const float pj = lane < n ? __expf(s - m_new) : 0.0f;
-      const float corr = __expf(m - m_new);
-      l = l * corr + wave_sum(pj);
-      m = m_new;
+    float o[16][4];
 #pragma unroll
-      for (int c = 0; c < 8; ++c)
-        acc[c] *= corr;
-      for (unsigned j = 0; j < n; ++j) {
-        const float pb = __shfl_sync(0xffffffffu, pj, j);
-        const uint4 raw = vs[j][lane];
-        const __half2* hv = reinterpret_cast<const __half2*>(&raw);
+    for (int mb = 0; mb < 16; ++mb)
+      o[mb][0] = o[mb][1] = o[mb][2] = o[mb][3] = 0.0f;
+    float m0 = kNegInf, m1 = kNegInf, l0 = 0.0f, l1 = 0.0f;
+
+    // K rows g, g + 8 of a slab: dims [64 tq, +64) as 8 x 16 bytes each; V rows 2 tq, 2 tq + 1,
+    // 2 tq + 8, 2 tq + 9: dims [32 g, +32) as 4 x 16 bytes each. Rows at or past j_end are not
+    // read (zero).
+    uint4 kr[2][8], vr[4][4];
+    auto load_k = [&](unsigned s) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const float2 vf = __half22float2(hv[c]);
-          acc[2 * c] += pb * vf.x;
-          acc[2 * c + 1] += pb * vf.y;
-        }
+      for (int r = 0; r < 2; ++r) {
+        const unsigned key = j_begin + kSlab * s + g + 8 * r;
+        const half_t* row = K + std::size_t{key} * kDim + 64 * tq;
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          kr[r][c] = key < j_end ? dev::ld_stream16(row + 8 * c, policy) : make_uint4(0, 0, 0, 0);
       }
-      __syncthreads();
+    };
+    auto load_v = [&](unsigned s) {
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const unsigned key = j_begin + kSlab * s + 2 * tq + (r & 1) + 8 * (r >> 1);
+        const half_t* row = V + std::size_t{key} * kDim + 32 * g;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          vr[r][c] = key < j_end ? dev::ld_stream16(row + 8 * c, policy) : make_uint4(0, 0, 0, 0);
+      }
+    };
+    auto word = [](const uint4& v, int i) -> uint32_t {
+      return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+    };
+
+    if (warp < nslab) {
+      load_k(warp);
+      load_v(warp);
     }
-    const std::size_t base = (std::size_t{kvh} * p.n_splits + split) * kGroup + h;
-    if (lane == 0)
-      p.part_m[base] = m, p.part_l[base] = l;
-    float4* o4 = reinterpret_cast<float4*>(p.part_o + base * kDim + 8 * lane);
-    o4[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-    o4[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    for (unsigned s = warp; s < nslab; s += kWarps) {
+      const unsigned key0 = j_begin + kSlab * s;
+      // ---- S^T = K Q^T (hi and lo query parts in separate accumulators) ----------------------
+      float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int ks = 0; ks < 16; ++ks) {
+        const uint32_t a0 = word(kr[0][ks / 2], 2 * (ks % 2));
+        const uint32_t a2 = word(kr[0][ks / 2], 2 * (ks % 2) + 1);
+        const uint32_t a1 = word(kr[1][ks / 2], 2 * (ks % 2));
+        const uint32_t a3 = word(kr[1][ks / 2], 2 * (ks % 2) + 1);
+        const uint4 qf = qfrag[ks][lane];
+        dev::mma_f16(sa, a0, a1, a2, a3, qf.x, qf.y);
+        dev::mma_f16(sb, a0, a1, a2, a3, qf.z, qf.w);
+      }
+      if (s + kWarps < nslab)
+        load_k(s + kWarps);  // the K registers are free: start the next slab's keys
+      float sv[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+        sv[r] = sa[r] + sb[r];
+      // sv[0], sv[1]: key g, heads 2 tq, 2 tq + 1; sv[2], sv[3]: key g + 8.
+      if (key0 + g >= j_end)
+        sv[0] = sv[1] = kNegInf;
+      if (key0 + g + 8 >= j_end)
+        sv[2] = sv[3] = kNegInf;
+      float mx0 = fmaxf(sv[0], sv[2]), mx1 = fmaxf(sv[1], sv[3]);
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+      }
+      const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);  // finite: key0 < j_end
+      const float c0 = __expf(m0 - mn0), c1 = __expf(m1 - mn1);
+      const float p0 = sv[0] == kNegInf ? 0.0f : __expf(sv[0] - mn0);
+      const float p1 = sv[1] == kNegInf ? 0.0f : __expf(sv[1] - mn1);
+      const float p2 = sv[2] == kNegInf ? 0.0f : __expf(sv[2] - mn0);
+      const float p3 = sv[3] == kNegInf ? 0.0f : __expf(sv[3] - mn1);
+      l0 = l0 * c0 + (p0 + p2);
+      l1 = l1 * c1 + (p1 + p3);
+      m0 = mn0, m1 = mn1;
+#pragma unroll
+      for (int mb = 0; mb < 16; ++mb)
+        o[mb][0] *= c0, o[mb][1] *= c1, o[mb][2] *= c0, o[mb][3] *= c1;
+      uint32_t h01, lo01, h23, lo23;
+      dev::split_half2(p0, p1, h01, lo01);
+      dev::split_half2(p2, p3, h23, lo23);
+      const uint32_t bh0 = dev::movmatrix_t(h01), bh1 = dev::movmatrix_t(h23);
+      const uint32_t bl0 = dev::movmatrix_t(lo01), bl1 = dev::movmatrix_t(lo23);
+      // ---- O^T += V^T P^T: m-block mb, row g = dim 32 g + 2 mb, row g + 8 = the next dim -------
+#pragma unroll
+      for (int mb = 0; mb < 16; ++mb) {
+        const uint32_t w0 = word(vr[0][mb / 4], mb % 4), w1 = word(vr[1][mb / 4], mb % 4);
+        const uint32_t w2 = word(vr[2][mb / 4], mb % 4), w3 = word(vr[3][mb / 4], mb % 4);
+        const uint32_t a0 = dev::prmt(w0, w1, 0x5410), a1 = dev::prmt(w0, w1, 0x7632);
+        const uint32_t a2 = dev::prmt(w2, w3, 0x5410), a3 = dev::prmt(w2, w3, 0x7632);
+        dev::mma_f16(o[mb], a0, a1, a2, a3, bh0, bh1);
+        dev::mma_f16(o[mb], a0, a1, a2, a3, bl0, bl1);
+      }
+      if (s + kWarps < nslab)
+        load_v(s + kWarps);
+    }
+
+    // ---- merge the eight warp states (tree through two shared-memory slots) -------------------
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+      l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+      l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+    }
+    if (g == 0)
+      red_m[warp][2 * tq] = m0, red_m[warp][2 * tq + 1] = m1;
     __syncthreads();
+    float M0 = kNegInf, M1 = kNegInf;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      M0 = fmaxf(M0, red_m[w][2 * tq]);
+      M1 = fmaxf(M1, red_m[w][2 * tq + 1]);
+    }
+    const float sc0 = m0 == kNegInf ? 0.0f : __expf(m0 - M0);
+    const float sc1 = m1 == kNegInf ? 0.0f : __expf(m1 - M1);
+    l0 *= sc0, l1 *= sc1;
+#pragma unroll
+    for (int mb = 0; mb < 16; ++mb)
+      o[mb][0] *= sc0, o[mb][1] *= sc1, o[mb][2] *= sc0, o[mb][3] *= sc1;
+    auto put = [&](int si) {
+      float* sl = slot[si];
+#pragma unroll
+      for (int mb = 0; mb < 16; ++mb) {
+        const unsigned d = 32 * g + 2 * mb;
+        sl[split_slot_index(2 * tq, d)] = o[mb][0];
+        sl[split_slot_index(2 * tq + 1, d)] = o[mb][1];
+        sl[split_slot_index(2 * tq, d + 1)] = o[mb][2];
+        sl[split_slot_index(2 * tq + 1, d + 1)] = o[mb][3];
+      }
+      if (g == 0)
+        sl[8 * attn_detail::kSplitSlotHead + 2 * tq] = l0,
+        sl[8 * attn_detail::kSplitSlotHead + 2 * tq + 1] = l1;
+    };
+    auto take = [&](int si) {
+      const float* sl = slot[si];
+#pragma unroll
+      for (int mb = 0; mb < 16; ++mb) {
+        const unsigned d = 32 * g + 2 * mb;
+        o[mb][0] += sl[split_slot_index(2 * tq, d)];
+        o[mb][1] += sl[split_slot_index(2 * tq + 1, d)];
+        o[mb][2] += sl[split_slot_index(2 * tq, d + 1)];
+        o[mb][3] += sl[split_slot_index(2 * tq + 1, d + 1)];
+      }
+      l0 += sl[8 * attn_detail::kSplitSlotHead + 2 * tq];
+      l1 += sl[8 * attn_detail::kSplitSlotHead + 2 * tq + 1];
+    };
+    // (w0 + w4) (w1 + w5), (w2 + w6) (w3 + w7), (w0 + w2) (w1 + w3); then slots hold w0, w1.
+    if (warp == 4 || warp == 5) put(warp - 4);
+    __syncthreads();
+    if (warp == 0 || warp == 1) take(warp);
+    __syncthreads();
+    if (warp == 6 || warp == 7) put(warp - 6);
+    __syncthreads();
+    if (warp == 2 || warp == 3) take(warp - 2);
+    __syncthreads();
+    if (warp == 2 || warp == 3) put(warp - 2);
+    __syncthreads();
+    if (warp == 0 || warp == 1) take(warp);
+    __syncthreads();
+    if (warp == 0 || warp == 1) put(warp);
+    __syncthreads();
+    // Write the split's triple: thread (h = tid / 32, dims 8 (tid % 32) .. + 7).
+    {
+      const unsigned h = tid / 32, d0 = 8 * (tid % 32);
+      const std::size_t base = (std::size_t{kvh} * p.n_splits + split) * kGroup + h;
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        v[e] = slot[0][split_slot_index(h, d0 + e)] + slot[1][split_slot_index(h, d0 + e)];
+      float4* o4 = reinterpret_cast<float4*>(p.part_o + base * kDim + d0);
+      o4[0] = make_float4(v[0], v[1], v[2], v[3]);
+      o4[1] = make_float4(v[4], v[5], v[6], v[7]);
+      if (tid % 32 == 0) {
+        float M = kNegInf;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w)
+          M = fmaxf(M, red_m[w][h]);
+        p.part_m[base] = M;
+        p.part_l[base] = slot[0][8 * attn_detail::kSplitSlotHead + h] +
+                         slot[1][8 * attn_detail::kSplitSlotHead + h];
+      }
+    }
+    __syncthreads();  // slots, red_m and qfrag free for the next item
   }
 }
 
