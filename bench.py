@@ -105,19 +105,33 @@ class Clocks:
 # ------------------------------------------------------------------------------- reference arm
 
 
-def cpu_decode_sample(lens: np.ndarray, seqs: list[int], seed: int, threads: int):
-    """Host data for a sample of sequences and a callable that runs the oracle decode on it."""
+CPU_SAMPLE = ("the whole batch of {b} sequences per step (the GPU arm's lens), fp64 restatement "
+              "of the reference's decode reference (tests/test_attn_splitk.hip:153-173)")
+
+
+def cpu_decode_batch(lens: np.ndarray, seed: int, threads: int):
+    """Host data for one decode step of the whole batch (K / V N(0, 1) fp16, q, gate N(0, 1)) and
+    a callable that runs the oracle decode on it. Both CPU figures of the benchmark (the
+    reference arm and the GPU arm's cpu_baseline) time this same callable."""
     import oracle
-    rng = np.random.RandomState(seed)
-    sub = lens[seqs]
-    cap = int(sub.max())
-    rows = len(seqs) * KV_HEADS * cap
-    k = rng.standard_normal((rows, DIM)).astype(np.float16).view(np.uint16)
-    v = rng.standard_normal((rows, DIM)).astype(np.float16).view(np.uint16)
-    kv_row = (np.arange(len(seqs) * KV_HEADS, dtype=np.int64) * cap).reshape(-1, KV_HEADS)
-    q = rng.standard_normal((len(seqs), Q_HEADS, DIM)).astype(np.float32)
-    qg = rng.standard_normal((len(seqs), Q_HEADS, 2 * DIM)).astype(np.float32)
-    return lambda: oracle.attn_decode(q, qg, Q_HEADS * 2 * DIM, k, v, kv_row, sub,
+    rng = np.random.default_rng(seed)
+    b = len(lens)
+    cap = int(lens.max())
+    rows = b * KV_HEADS * cap
+    k = np.empty((rows, DIM), np.uint16)
+    v = np.empty((rows, DIM), np.uint16)
+    kv_row = (np.arange(b * KV_HEADS, dtype=np.int64) * cap).reshape(-1, KV_HEADS)
+    for i in range(b * KV_HEADS):  # only the rows each sequence uses are filled
+        n = int(lens[i // KV_HEADS])
+        r0 = i * cap
+        k[r0:r0 + n] = rng.standard_normal((n, DIM), dtype=np.float32).astype(np.float16).view(
+            np.uint16)
+        v[r0:r0 + n] = rng.standard_normal((n, DIM), dtype=np.float32).astype(np.float16).view(
+            np.uint16)
+    q = rng.standard_normal((b, Q_HEADS, DIM), dtype=np.float32)
+    qg = rng.standard_normal((b, Q_HEADS, 2 * DIM), dtype=np.float32)
+    lens = np.ascontiguousarray(lens, np.int32)
+    return lambda: oracle.attn_decode(q, qg, Q_HEADS * 2 * DIM, k, v, kv_row, lens,
                                       threads=threads)
 
 
@@ -128,19 +142,16 @@ def run_reference(args) -> None:
     import oracle
     oracle.build()
     threads = oracle.cpu_count()
-    lens = lens_config()
-    per_step = 4  # sequences per step: a bounded sample of the batch
+    fn = cpu_decode_batch(lens_config(), seed=100, threads=threads)
     steps = []
     for i in range(args.warmup + args.steps):
-        seqs = [(i * per_step + j) % BATCH for j in range(per_step)]
-        fn = cpu_decode_sample(lens, seqs, seed=100 + i, threads=threads)
         t0 = time.perf_counter()
         fn()
         dt = time.perf_counter() - t0
         if i >= args.warmup:
             steps.append(dt)
     t = sum(steps) / len(steps)
-    value = per_step / t
+    value = BATCH / t
     line = {
         "impl": "reference", "metric": "attn decode tok/s", "value": value, "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -148,8 +159,7 @@ def run_reference(args) -> None:
         "vs_baseline": None, "dtype": "f64", "data": "synthetic",
         "config": workload_config(args.gpus),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": f"{per_step} of the {BATCH} sequences per step (rotating), "
-                                   "fp64 restatement of the reference's decode reference"},
+                         "sample": CPU_SAMPLE.format(b=BATCH)},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -166,6 +176,209 @@ def workload_config(n_gpus: int) -> dict:
 
 
 # ------------------------------------------------------------------------------------- miso arm
+
+
+class DecodeBatch:
+    """A batch of sequences in one KV pool (fp16 N(0, 1), lens given, `extra` free rows per
+    sequence for appended tokens), their projection rows and the two launches of a decode step:
+    batched prep (norms, RoPE, KV append, lens advance) and the stream-K split-K decode."""
+
+    def __init__(self, dev, lens: np.ndarray, extra: int, seed: int, stream):
+        import torch
+        from miso_b200 import attention as A
+        from miso_b200 import capi
+        self.capi, self.lib, self.stream = capi, capi.load(), stream
+        self.batch = b = len(lens)
+        self.lens0 = lens.astype(np.int64)
+        seg_caps = np.repeat(self.lens0 + extra, KV_HEADS)
+        starts = np.concatenate([[0], np.cumsum(seg_caps)[:-1]]).astype(np.int64)
+        self.rows = rows = int(seg_caps.sum())
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        pool = A.KvPool.__new__(A.KvPool)
+        pool.batch, pool.capacity, pool.rows = b, None, rows
+        pool.k = torch.randn((rows, DIM), generator=g, device=dev, dtype=torch.float16)
+        pool.v = torch.randn((rows, DIM), generator=g, device=dev, dtype=torch.float16)
+        pool.kv_row = torch.from_numpy(starts.reshape(b, KV_HEADS)).to(dev)
+        pool.lens = torch.from_numpy(lens.astype(np.int32)).to(dev)
+        self.pool = pool
+        self.proj = torch.randn((b, PROJ), generator=g, device=dev, dtype=torch.float32)
+        self.q_norm = (1.0 + 0.1 * torch.randn(DIM, generator=g, device=dev)).float()
+        self.k_norm = (1.0 + 0.1 * torch.randn(DIM, generator=g, device=dev)).float()
+        self.inv_freq = torch.from_numpy(A.rope_inv_freq()).to(dev)
+        self.q = torch.empty((b, Q_HEADS, DIM), device=dev)
+        self.core = torch.empty((b, Q_HEADS, DIM), device=dev)
+        self.scratch = A.decode_scratch(b, device=dev)
+
+    def prep(self, src_base: int):
+        capi, pool = self.capi, self.pool
+        p = capi.AttnPrepBatchedParams(src_base, src_base + 8192 * 4, src_base + 8704 * 4,
+                                       self.q_norm.data_ptr(), self.k_norm.data_ptr(),
+                                       self.inv_freq.data_ptr(), pool.k.data_ptr(),
+                                       pool.v.data_ptr(), pool.kv_row.data_ptr(),
+                                       pool.lens.data_ptr(), self.q.data_ptr(), self.batch, PROJ,
+                                       EPS)
+        capi.check("miso_attn_prep_batched",
+                   self.lib.miso_attn_prep_batched(ctypes.byref(p), self.stream.cuda_stream))
+
+    def decode(self, qg_base: int, out=None, kv_row=None):
+        capi, pool = self.capi, self.pool
+        out = self.core if out is None else out
+        kv_row = pool.kv_row.data_ptr() if kv_row is None else kv_row
+        dp = capi.AttnDecodeParams(self.q.data_ptr(), qg_base, pool.k.data_ptr(),
+                                   pool.v.data_ptr(), kv_row, pool.lens.data_ptr(),
+                                   out.data_ptr(), self.rows, self.batch, PROJ)
+        capi.check("miso_attn_decode",
+                   self.lib.miso_attn_decode(ctypes.byref(dp), self.scratch.data_ptr(),
+                                             self.scratch.numel() * 4, self.stream.cuda_stream))
+
+    def time_device(self, steps: int, warmup: int, barrier):
+        """Device-resident decode steps (prep + decode) timed with CUDA events: returns (step ms,
+        decode-kernel ms, algorithmic bytes per decode launch), averaged over the timed steps.
+        The bytes: K and V of every cached position (after the step's append), q and gate
+        reads and the output write."""
+        import torch
+        stream, base = self.stream, self.proj.data_ptr()
+        for _ in range(warmup):
+            self.prep(base)
+            self.decode(base)
+        torch.cuda.synchronize()
+        lens_start = self.pool.lens.cpu().numpy().astype(np.int64)
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(steps)]
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize()
+        start.record(stream)
+        for i in range(steps):
+            self.prep(base)
+            ev[i][0].record(stream)
+            self.decode(base)
+            ev[i][1].record(stream)
+        end.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        dec_ms = sum(a.elapsed_time(b) for a, b in ev) / steps
+        nbytes = sum(float(((lens_start + i + 1) * KV_BYTES_PER_POS).sum() +
+                           self.batch * QGO_BYTES_PER_SEQ) for i in range(steps)) / steps
+        return start.elapsed_time(end) / steps, dec_ms, nbytes
+
+
+def bench_decode_32k(args, dev, stream, max_over_ranks, barrier, world, rank) -> dict:
+    """BASELINE's "@32k ctx" decode figure: config 2 with every sequence at 32768 cached
+    positions (32 sequences per GPU, 2.147 GB of K / V per step)."""
+    b = args.batch
+    db = DecodeBatch(dev, np.full(b, 32768, np.int32), args.warmup + args.steps + 4,
+                     4321 + rank, stream)
+    step_ms, dec_ms, nbytes = db.time_device(args.steps, args.warmup, barrier)
+    step_ms, dec_ms = max_over_ranks(step_ms), max_over_ranks(dec_ms)
+    pk = peaks()
+    achieved = nbytes / (dec_ms * 1e-3) / 1e9
+    return {"metric": "attn decode tok/s @32k ctx", "value": world * b / (step_ms * 1e-3),
+            "unit": "tokens/s", "ms_per_step": step_ms, "batch_per_gpu": b, "ctx_len": 32768,
+            "bytes_per_step": nbytes, "gbs": achieved,
+            "config": "config 2 shapes with all lens = 32768; step = batched prep + split-K "
+                      "decode (inputs larger than L2)",
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"],
+                         "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
+                         "traffic": nbytes * DECODE_TRAFFIC_PER_ALGORITHMIC_BYTE,
+                         "kernel": "decode_kernel", "kernel_ms": dec_ms,
+                         "peak_source": pk["source"]},
+            "gpu_launches": 2 * args.steps}
+
+
+C1_CTX = 4096
+C1_COPIES = 32  # 32 x 8.4 MB of K / V rotate, so a step never finds its cache in the 126 MB L2
+
+
+def bench_decode_config1(args, dev, stream, max_over_ranks, barrier, world, rank) -> dict:
+    """one sequence, 16 Q / 2 KV heads, head_dim 256, context 4096, fp16 K / V
+    cache and fp32 queries N(0, 1), fp32 output [16][256] (the reference's CPU-runnable decode
+    step). One step = the attention decode over the cache. 32 copies of the cache rotate from
+    step to step so that the 8.4 MB are read from HBM, not L2. Timed two ways: the fast
+    stream-K decode (one launch), and the drop-in split + combine pair that the reference
+    engine launches (miso_attn_split / miso_attn_combine, caller geometry). Steps are captured
+    in a CUDA graph so that the host's launch cost does not pace a single sequence."""
+    import torch
+    from miso_b200 import attention as A
+    from miso_b200 import capi
+    lib = capi.load()
+    db = DecodeBatch(dev, np.full(C1_COPIES, C1_CTX, np.int32), 0, 777 + rank, stream)
+    # batch 1 over the pool: copy c is pool rows kv_row[c]
+    kv_rows = db.pool.kv_row.contiguous()
+    lens1 = torch.full((1,), C1_CTX, dtype=torch.int32, device=dev)
+    db.pool.lens = lens1
+    db.batch = 1
+    q = torch.randn((1, Q_HEADS, DIM), device=dev)
+    db.q = q
+    qg = db.proj[:1]
+    out = torch.empty((1, Q_HEADS, DIM), device=dev)
+    ns = A.n_splits(C1_CTX, A.MAX_SPLITS)
+    sc = A.AttentionScratch(device=dev)
+    # a reference AttentionCache per copy: the pool's two KV-head segments of copy c are
+    # [2][C1_CTX][256] contiguous (capacity C1_CTX, no extra rows)
+    seg = C1_CTX * DIM * 2
+
+    def fast(i, st):
+        db.stream = st
+        db.decode(qg.data_ptr(), out, kv_rows.data_ptr() + (i % C1_COPIES) * 16)
+
+    def drop_in(i, st):
+        c = i % C1_COPIES
+        kb = db.pool.k.data_ptr() + 2 * c * seg
+        vb = db.pool.v.data_ptr() + 2 * c * seg
+        sp = capi.AttnSplitParams(q.data_ptr(), kb, vb, sc.part_m.data_ptr(),
+                                  sc.part_l.data_ptr(), sc.part_o.data_ptr(), C1_CTX, C1_CTX, ns)
+        capi.check("miso_attn_split", lib.miso_attn_split(ctypes.byref(sp), st.cuda_stream))
+        cp_ = capi.AttnCombineParams(sc.part_m.data_ptr(), sc.part_l.data_ptr(),
+                                     sc.part_o.data_ptr(), qg.data_ptr(), out.data_ptr(), ns)
+        capi.check("miso_attn_combine", lib.miso_attn_combine(ctypes.byref(cp_), st.cuda_stream))
+
+    def timed(fn) -> float:
+        n = max(args.steps, C1_COPIES)
+        for i in range(max(args.warmup, C1_COPIES)):
+            fn(i, stream)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        cap = torch.cuda.Stream(device=dev)
+        cap.wait_stream(stream)
+        with torch.cuda.graph(graph, stream=cap):
+            for i in range(n):
+                fn(i, cap)
+        graph.replay()
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            graph.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        del graph
+        return max_over_ranks(e0.elapsed_time(e1) / n)
+
+    fast_ms = timed(fast)
+    drop_ms = timed(drop_in)
+    nbytes = C1_CTX * KV_BYTES_PER_POS + QGO_BYTES_PER_SEQ
+    pk = peaks()
+    a_fast = nbytes / (fast_ms * 1e-3) / 1e9
+    return {"metric": "attn decode tok/s, 1 sequence @4096 ctx (config 1)",
+            "value": world / (fast_ms * 1e-3), "unit": "tokens/s", "ms_per_step": fast_ms,
+            "bytes_per_step": nbytes, "gbs": a_fast,
+            "drop_in": {"ms_per_step": drop_ms, "value": world / (drop_ms * 1e-3),
+                        "gbs": nbytes / (drop_ms * 1e-3) / 1e9, "n_splits": ns,
+                        "launches": "attn_split_kernel<256> (n_splits x 2) + "
+                                    "attn_combine_kernel<64, true, 4>"},
+            "config": "BASELINE config 1: 1 sequence, ctx 4096, fp16 KV, fp32 q, gate; 32 "
+                      "rotating cache copies (268 MB > L2); steps replayed from a CUDA graph",
+            "roofline": {"bound": "hbm", "achieved": a_fast, "peak": pk["hbm_gbs"],
+                         "unit": "GB/s", "frac": a_fast / pk["hbm_gbs"], "traffic": None,
+                         "kernel": "decode_kernel", "kernel_ms": fast_ms,
+                         "peak_source": pk["source"],
+                         "note": "8.4 MB per step: launch- and latency-bound, far from the HBM "
+                                 "roofline by construction"},
+            "gpu_launches": 2 * max(args.steps, C1_COPIES) * 3}
 
 
 def run_miso(args) -> None:
@@ -187,52 +400,7 @@ def run_miso(args) -> None:
     from miso_b200 import capi
 
     lens0 = lens_config()
-    # Room for the appended tokens: the device-timed loop and the end-to-end loop each append
-    # warmup + steps tokens to every sequence.
-    extra = 2 * (args.warmup + args.steps) + 4
-    caps = (lens0.astype(np.int64) + extra)
-    seg_caps = np.repeat(caps, KV_HEADS)
-    starts = np.concatenate([[0], np.cumsum(seg_caps)[:-1]]).astype(np.int64)
-    rows = int(seg_caps.sum())
-
-    g = torch.Generator(device=dev)
-    g.manual_seed(1234 + rank)
-    pool = A.KvPool.__new__(A.KvPool)
-    pool.batch, pool.capacity, pool.rows = BATCH, None, rows
-    pool.k = torch.randn((rows, DIM), generator=g, device=dev, dtype=torch.float16)
-    pool.v = torch.randn((rows, DIM), generator=g, device=dev, dtype=torch.float16)
-    pool.kv_row = torch.from_numpy(starts.reshape(BATCH, KV_HEADS)).to(dev)
-    pool.lens = torch.from_numpy(lens0.copy()).to(dev)
-
-    proj = torch.randn((BATCH, PROJ), generator=g, device=dev, dtype=torch.float32)
-    q_norm = (1.0 + 0.1 * torch.randn(DIM, generator=g, device=dev)).float()
-    k_norm = (1.0 + 0.1 * torch.randn(DIM, generator=g, device=dev)).float()
-    inv_freq = torch.from_numpy(A.rope_inv_freq()).to(dev)
-    q = torch.empty((BATCH, Q_HEADS, DIM), device=dev)
-    core = torch.empty((BATCH, Q_HEADS, DIM), device=dev)
-    scratch = A.decode_scratch(BATCH, device=dev)
     stream = torch.cuda.current_stream(dev)
-    base = proj.data_ptr()
-
-    def step(src_base: int):
-        p = capi.AttnPrepBatchedParams(src_base, src_base + 8192 * 4, src_base + 8704 * 4,
-                                       q_norm.data_ptr(), k_norm.data_ptr(), inv_freq.data_ptr(),
-                                       pool.k.data_ptr(), pool.v.data_ptr(),
-                                       pool.kv_row.data_ptr(), pool.lens.data_ptr(),
-                                       q.data_ptr(), BATCH, PROJ, EPS)
-        capi.check("miso_attn_prep_batched",
-                   capi.load().miso_attn_prep_batched(ctypes.byref(p),
-                                                      stream.cuda_stream))
-
-    def decode(qg_base: int, out=None):
-        out = core if out is None else out
-        dp = capi.AttnDecodeParams(q.data_ptr(), qg_base, pool.k.data_ptr(), pool.v.data_ptr(),
-                                   pool.kv_row.data_ptr(), pool.lens.data_ptr(), out.data_ptr(),
-                                   rows, BATCH, PROJ)
-        capi.check("miso_attn_decode",
-                   capi.load().miso_attn_decode(ctypes.byref(dp),
-                                                scratch.data_ptr(),
-                                                scratch.numel() * 4, stream.cuda_stream))
 
     def barrier():
         if world > 1:
@@ -245,36 +413,17 @@ def run_miso(args) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    # Room for the appended tokens: the device-timed loop and the end-to-end loop each append
+    # warmup + steps tokens to every sequence.
+    db = DecodeBatch(dev, lens0, 2 * (args.warmup + args.steps) + 4, 1234 + rank, stream)
+    step, decode, base = db.prep, db.decode, db.proj.data_ptr()
+    pool = db.pool
+
     # ---- device-resident timing ---------------------------------------------------------------
-    for _ in range(args.warmup):
-        step(base)
-        decode(base)
-    torch.cuda.synchronize()
-    lens_start = pool.lens.cpu().numpy().astype(np.int64)
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(args.steps)]
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    torch.cuda.synchronize()
     with Clocks(local) as clk:
-        start.record(stream)
-        for i in range(args.steps):
-            step(base)
-            ev[i][0].record(stream)
-            decode(base)
-            ev[i][1].record(stream)
-        end.record(stream)
-        torch.cuda.synchronize()
-    barrier()
-    step_ms = start.elapsed_time(end) / args.steps
-    dec_ms = [a.elapsed_time(b) for a, b in ev]
+        step_ms, dec_avg_ms, dec_bytes = db.time_device(args.steps, args.warmup, barrier)
     step_ms_max = max_over_ranks(step_ms)
-    # Algorithmic bytes of each decode launch: every position of every sequence, K and V, plus
-    # q / gate reads and the output write.
-    dec_bytes = [float(((lens_start + i + 1) * KV_BYTES_PER_POS).sum() + BATCH * QGO_BYTES_PER_SEQ)
-                 for i in range(args.steps)]
-    dec_avg_ms = sum(dec_ms) / len(dec_ms)
-    achieved = (sum(dec_bytes) / len(dec_bytes)) / (dec_avg_ms * 1e-3) / 1e9
+    achieved = dec_bytes / (dec_avg_ms * 1e-3) / 1e9
     pk = peaks()
 
     # ---- end to end through the C ABI with host buffers ---------------------------------------
@@ -333,6 +482,12 @@ def run_miso(args) -> None:
     assert torch.equal(host_out[last], dev_out[last].cpu()), "end-to-end download mismatch"
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
 
+    decode_32k = None if args.no_decode_legs else bench_decode_32k(args, dev, stream,
+                                                                   max_over_ranks, barrier,
+                                                                   world, rank)
+    decode_c1 = None if args.no_decode_legs else bench_decode_config1(args, dev, stream,
+                                                                      max_over_ranks, barrier,
+                                                                      world, rank)
     prefill = None if args.no_prefill else bench_prefill(args, dev, stream, max_over_ranks,
                                                          barrier, world)
     dn_step = None if args.no_deltanet else bench_deltanet_step(args, dev, stream,
@@ -353,8 +508,7 @@ def run_miso(args) -> None:
         import oracle
         oracle.build()
         threads = oracle.cpu_count()
-        per = 8
-        fn = cpu_decode_sample(lens0, list(range(per)), seed=7, threads=threads)
+        fn = cpu_decode_batch(lens0, seed=100, threads=threads)
         fn()
         t0 = time.perf_counter()
         reps = 0
@@ -364,10 +518,8 @@ def run_miso(args) -> None:
             if time.perf_counter() - t0 > 10.0 or reps >= 20:
                 break
         t = (time.perf_counter() - t0) / reps
-        cpu = {"value": per / t, "unit": "tokens/s", "cores": threads, "kind": "port",
-               "sample": f"sequences 0-{per - 1} of the batch (lens {int(lens0[:per].min())}-"
-                         f"{int(lens0[:per].max())}), {reps} repetitions, fp64 restatement of "
-                         "the reference decode (tests/test_attn_splitk.hip:153-173)"}
+        cpu = {"value": BATCH / t, "unit": "tokens/s", "cores": threads, "kind": "port",
+               "sample": CPU_SAMPLE.format(b=BATCH) + f", {reps} steps"}
 
     if world > 1:
         dist.barrier()
@@ -382,8 +534,7 @@ def run_miso(args) -> None:
         "data": "synthetic", "config": workload_config(world),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"],
                      "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
-                     "traffic": (sum(dec_bytes) / len(dec_bytes)) *
-                                DECODE_TRAFFIC_PER_ALGORITHMIC_BYTE,
+                     "traffic": dec_bytes * DECODE_TRAFFIC_PER_ALGORITHMIC_BYTE,
                      "traffic_source": "ncu dram read + write of a batch-8 capture "
                                        "(profiles/decode_kernel_b8_ncu.md) scaled by the KV "
                                        "bytes of a full launch",
@@ -395,6 +546,8 @@ def run_miso(args) -> None:
         "gpu_launches": 2 * args.steps,
         "clocks": clk.summary(),
         "cpu_baseline": cpu,
+        "decode_32k": decode_32k,
+        "decode_config1": decode_c1,
         "prefill": prefill,
         "deltanet_step": dn_step,
         "deltanet_prefill": dn_prefill,
@@ -858,6 +1011,8 @@ def main():
     ap.add_argument("--cp-decode-steps", type=int, default=CP_DEC_STEPS,
                     help="decode steps of the config 5 block after the prefix")
     ap.add_argument("--no-cp", action="store_true", help="skip the config 5 block")
+    ap.add_argument("--no-decode-legs", action="store_true",
+                    help="skip the fixed-32k and config-1 decode legs")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
