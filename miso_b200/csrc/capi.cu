@@ -20,7 +20,7 @@
 #include "fast/attn_prefill_tc.cuh"
 #include "fast/attn_prep.cuh"
 #include "fast/deltanet_step_batched.cuh"
-#include "fast/deltanet_chunk_tc.cuh"
+#include "fast/deltanet_prefill_tc.cuh"
 #include "kernels/attention_decode.hpp"
 #include "kernels/attention_prefill.hpp"
 #include "kernels/deltanet_chunk.hpp"
@@ -117,13 +117,13 @@ int device_info(DeviceInfo** out) {
                                cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(miso::fast::prefill::kSmemBytes));
     if (a == cudaSuccess)
-      a = cudaFuncSetAttribute(miso::fast::dnchunk::prepare_kernel,
+      a = cudaFuncSetAttribute(miso::fast::dnpf::front_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(miso::fast::dnchunk::kPrepSmemBytes));
+                               static_cast<int>(miso::fast::dnpf::kFrontSmemBytes));
     if (a == cudaSuccess)
-      a = cudaFuncSetAttribute(miso::fast::dnchunk::recur_kernel,
+      a = cudaFuncSetAttribute(miso::fast::dnpf::chain_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(miso::fast::dnchunk::kRecurSmemBytes));
+                               static_cast<int>(miso::fast::dnpf::kChainSmemBytes));
     d.status = a == cudaSuccess ? MISO_OK : static_cast<int>(a);
   });
   *out = &d;
@@ -163,6 +163,17 @@ int f16_map(CUtensorMap* map, const void* ptr, cuuint32_t rank, const cuuint64_t
   const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, rank, const_cast<void*>(ptr),
                               dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? MISO_OK : MISO_ERR_INVALID;
+}
+
+// 2-D fp32 tensor map without swizzle; dims / box innermost first, row stride in bytes.
+int f32_map(CUtensorMap* map, const void* ptr, const cuuint64_t* dims, const cuuint64_t* strides,
+            const cuuint32_t* box) {
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(ptr),
+                              dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? MISO_OK : MISO_ERR_INVALID;
 }
@@ -539,61 +550,55 @@ int miso_deltanet_step_batched(const miso_deltanet_step_batched_params* p, void*
   return launch_status();
 }
 
-// Scratch of miso_deltanet_prefill_tc, each part 1024-byte aligned: q16, k16 [n][16][128] and
-// v16 [n][32][128] fp16 with their fp16 remainders, beta, log_a, e^g [32][np] fp32, W, Ks, Qg
-// [32][nc][64][128] fp16, Tu, Aqk and its remainder [32][nc][64][64] fp16
-// (np = 64 nc, nc = ceil(n / 64)).
-struct DnChunkScratch {
-  size_t q16, k16, v16, q16lo, k16lo, v16lo, beta, loga, eg, w, ks, qg, tu, aqk, aqklo, total;
+// Scratch of miso_deltanet_prefill_tc: the per-(V head, chunk) records front_kernel writes and
+// chain_kernel reads, each part 1024-byte aligned (nc = ceil(n / 64)): Qg high and low parts and
+// W [32][nc][64][128] fp16, U [32][nc][64][128] fp32, [Ks^T; Aqk] high and low parts
+// [32][nc][192][64] fp16, e^(g_last) [32][nc] fp32.
+struct DnScratch {
+  size_t qgh, qgl, w, u, bh, bl, egl, total;
 };
 
-static DnChunkScratch dn_chunk_scratch(unsigned n) {
-  const size_t nc = (size_t(n) + 63) / 64, np = 64 * nc;
+static DnScratch dn_scratch(unsigned n) {
+  const size_t nc = (size_t(n) + 63) / 64;
   auto up = [](size_t x) { return (x + 1023) & ~size_t(1023); };
-  DnChunkScratch s;
+  DnScratch s;
   size_t o = 0;
-  s.q16 = o, o += up(size_t(n) * 16 * 128 * 2);
-  s.k16 = o, o += up(size_t(n) * 16 * 128 * 2);
-  s.v16 = o, o += up(size_t(n) * 32 * 128 * 2);
-  s.q16lo = o, o += up(size_t(n) * 16 * 128 * 2);
-  s.k16lo = o, o += up(size_t(n) * 16 * 128 * 2);
-  s.v16lo = o, o += up(size_t(n) * 32 * 128 * 2);
-  s.beta = o, o += up(32 * np * 4);
-  s.loga = o, o += up(32 * np * 4);
-  s.eg = o, o += up(32 * np * 4);
+  s.qgh = o, o += up(32 * nc * 64 * 128 * 2);
+  s.qgl = o, o += up(32 * nc * 64 * 128 * 2);
   s.w = o, o += up(32 * nc * 64 * 128 * 2);
-  s.ks = o, o += up(32 * nc * 64 * 128 * 2);
-  s.qg = o, o += up(32 * nc * 64 * 128 * 2);
-  s.tu = o, o += up(32 * nc * 64 * 64 * 2);
-  s.aqk = o, o += up(32 * nc * 64 * 64 * 2);
-  s.aqklo = o, o += up(32 * nc * 64 * 64 * 2);
+  s.u = o, o += up(32 * nc * 64 * 128 * 4);
+  s.bh = o, o += up(32 * nc * 192 * 64 * 2);
+  s.bl = o, o += up(32 * nc * 192 * 64 * 2);
+  s.egl = o, o += up(32 * nc * 4);
   s.total = o;
   return s;
 }
 
 size_t miso_deltanet_prefill_tc_scratch_bytes(unsigned n) {
-  return n == 0 ? 0 : dn_chunk_scratch(n).total;
+  return n == 0 ? 0 : dn_scratch(n).total;
 }
 
 }  // extern "C"
 
 namespace {
 
-// Stages of the tensor-core DeltaNet prefill: bit 0 = conv + prepare (no state access), bit 1 =
-// the recurrence (reads the scratch bit 0 wrote).
+// Stages of the tensor-core DeltaNet prefill: bit 0 = front_kernel (conv, norms and every
+// state-independent product of each chunk; no state access), bit 1 = chain_kernel (the state
+// recurrence and the outputs, from the records bit 0 wrote).
 int dn_prefill_tc(const miso_deltanet_seq_params* p, void* scratch, size_t scratch_bytes,
                   void* stream, int stages) {
-  namespace dc = miso::fast::dnchunk;
+  namespace pf = miso::fast::dnpf;
   if (p == nullptr || p->qkv == nullptr || p->z == nullptr || p->a == nullptr ||
       p->b == nullptr || p->conv_w == nullptr || p->conv_in == nullptr ||
       p->conv_out == nullptr || p->conv_in == p->conv_out || p->ssm_a == nullptr ||
       p->dt_bias == nullptr || p->norm_w == nullptr || p->state == nullptr ||
       p->out == nullptr || p->n == 0 || p->n > (1u << 24) || p->qkv_stride % 4 != 0 ||
-      p->qkv_stride < 8192 || p->zab_stride < 4160 || !aligned16(p->qkv) ||
-      !aligned16(p->state) || !aligned16(p->conv_w) || scratch == nullptr ||
+      p->qkv_stride < 8192 || p->zab_stride < 4160 || p->zab_stride % 4 != 0 ||
+      !aligned16(p->qkv) || !aligned16(p->state) || !aligned16(p->conv_w) ||
+      !aligned16(p->z) || !aligned16(p->norm_w) || !aligned16(p->out) || scratch == nullptr ||
       (reinterpret_cast<uintptr_t>(scratch) & 255u) != 0)
     return MISO_ERR_INVALID;
-  const DnChunkScratch L = dn_chunk_scratch(p->n);
+  const DnScratch L = dn_scratch(p->n);
   if (scratch_bytes < L.total)
     return MISO_ERR_SCRATCH;
   DeviceInfo* d = nullptr;
@@ -603,131 +608,93 @@ int dn_prefill_tc(const miso_deltanet_seq_params* p, void* scratch, size_t scrat
   if ((st = tensor_map_encoder()) != MISO_OK)
     return st;
   char* base = static_cast<char*>(scratch);
-  __half* q16 = reinterpret_cast<__half*>(base + L.q16);
-  __half* k16 = reinterpret_cast<__half*>(base + L.k16);
-  __half* v16 = reinterpret_cast<__half*>(base + L.v16);
-  __half* q16lo = reinterpret_cast<__half*>(base + L.q16lo);
-  __half* k16lo = reinterpret_cast<__half*>(base + L.k16lo);
-  __half* v16lo = reinterpret_cast<__half*>(base + L.v16lo);
-  float* beta = reinterpret_cast<float*>(base + L.beta);
-  float* loga = reinterpret_cast<float*>(base + L.loga);
-  float* eg = reinterpret_cast<float*>(base + L.eg);
-  __half* w = reinterpret_cast<__half*>(base + L.w);
-  __half* ks = reinterpret_cast<__half*>(base + L.ks);
-  __half* qg = reinterpret_cast<__half*>(base + L.qg);
-  __half* tu = reinterpret_cast<__half*>(base + L.tu);
-  __half* aqk = reinterpret_cast<__half*>(base + L.aqk);
-  __half* aqklo = reinterpret_cast<__half*>(base + L.aqklo);
-  const unsigned nc = (p->n + 63) / 64, np = 64 * nc;
-
-  CUtensorMap qmap, kmap, qlmap, klmap, vmap, vlmap, tumap, aqkmap, aqklmap, wmap, ksmap, qgmap;
-  {
-    const cuuint64_t dims[3] = {128, 16, p->n};
-    const cuuint64_t strides[2] = {128 * 2, 16 * 128 * 2};
-    const cuuint32_t box[3] = {64, 1, 64};
-    if ((st = f16_map(&qmap, q16, 3, dims, strides, box)) != MISO_OK ||
-        (st = f16_map(&kmap, k16, 3, dims, strides, box)) != MISO_OK ||
-        (st = f16_map(&qlmap, q16lo, 3, dims, strides, box)) != MISO_OK ||
-        (st = f16_map(&klmap, k16lo, 3, dims, strides, box)) != MISO_OK)
-      return st;
-  }
-  {
-    const cuuint64_t dims[3] = {128, 32, p->n};
-    const cuuint64_t strides[2] = {128 * 2, 32 * 128 * 2};
-    const cuuint32_t box[3] = {64, 1, 64};
-    if ((st = f16_map(&vmap, v16, 3, dims, strides, box)) != MISO_OK ||
-        (st = f16_map(&vlmap, v16lo, 3, dims, strides, box)) != MISO_OK)
-      return st;
-  }
-  {
-    const cuuint64_t dims[2] = {64, uint64_t(32) * nc * 64};
-    const cuuint64_t strides[1] = {64 * 2};
-    const cuuint32_t box[2] = {64, 64};
-    if ((st = f16_map(&tumap, tu, 2, dims, strides, box)) != MISO_OK ||
-        (st = f16_map(&aqkmap, aqk, 2, dims, strides, box)) != MISO_OK ||
-        (st = f16_map(&aqklmap, aqklo, 2, dims, strides, box)) != MISO_OK)
-      return st;
-  }
-  {
-    const cuuint64_t dims[2] = {128, uint64_t(32) * nc * 64};
-    const cuuint64_t strides[1] = {128 * 2};
-    const cuuint32_t box[2] = {64, 64};
-    if ((st = f16_map(&wmap, w, 2, dims, strides, box)) != MISO_OK ||
-        (st = f16_map(&ksmap, ks, 2, dims, strides, box)) != MISO_OK ||
-        (st = f16_map(&qgmap, qg, 2, dims, strides, box)) != MISO_OK)
-      return st;
-  }
+  const unsigned nc = (p->n + 63) / 64;
+  pf::Records rec;
+  rec.qgh = reinterpret_cast<__half*>(base + L.qgh);
+  rec.qgl = reinterpret_cast<__half*>(base + L.qgl);
+  rec.w = reinterpret_cast<__half*>(base + L.w);
+  rec.u = reinterpret_cast<float*>(base + L.u);
+  rec.bh = reinterpret_cast<__half*>(base + L.bh);
+  rec.bl = reinterpret_cast<__half*>(base + L.bl);
+  rec.egl = reinterpret_cast<float*>(base + L.egl);
   cudaStream_t s = as_stream(stream);
 
-  dc::ConvArgs ca;
-  ca.qkv = p->qkv;
-  ca.a = p->a;
-  ca.b = p->b;
-  ca.conv_w = p->conv_w;
-  ca.conv_in = p->conv_in;
-  ca.conv_out = p->conv_out;
-  ca.ssm_a = p->ssm_a;
-  ca.dt_bias = p->dt_bias;
-  ca.q16 = q16;
-  ca.k16 = k16;
-  ca.v16 = v16;
-  ca.q16lo = q16lo;
-  ca.k16lo = k16lo;
-  ca.v16lo = v16lo;
-  ca.beta = beta;
-  ca.loga = loga;
-  ca.n = p->n;
-  ca.np = np;
-  ca.qkv_stride = p->qkv_stride;
-  ca.zab_stride = p->zab_stride;
-
-  dc::PrepareArgs pa;
-  pa.beta = beta;
-  pa.loga = loga;
-  pa.eg = eg;
-  pa.w = w;
-  pa.ks = ks;
-  pa.qg = qg;
-  pa.tu = tu;
-  pa.aqk = aqk;
-  pa.aqklo = aqklo;
-  pa.n = p->n;
-  pa.np = np;
-  pa.nc = nc;
-
-  dc::RecurArgs ra;
-  ra.eg = eg;
-  ra.z = p->z;
-  ra.norm_w = p->norm_w;
-  ra.state = p->state;
-  ra.out = p->out;
-  ra.n = p->n;
-  ra.np = np;
-  ra.nc = nc;
-  ra.zab_stride = p->zab_stride;
-  ra.eps = p->eps;
-
-  // Three launches in stream order. (Overlapping the prepare kernel of later chunks with the
-  // recurrence of earlier ones on a second stream was measured slower: the recurrence is
-  // latency-bound and slows down next to other kernels, and every extra launch of it refills
-  // its pipeline.)
   if (stages & 1) {
-    ca.t_begin = 0;
-    dc::conv_kernel<<<dim3(8, (p->n + dc::kConvTokens - 1) / dc::kConvTokens), dc::kConvThreads,
-                      0, s>>>(ca);
-    if ((st = launch_status()) != MISO_OK)
-      return st;
-    pa.c_begin = 0;
-    dc::prepare_kernel<<<dim3(nc, 16), dc::kPrepThreads, dc::kPrepSmemBytes, s>>>(
-        qmap, kmap, qlmap, klmap, pa);
+    pf::FrontArgs fa;
+    fa.qkv = p->qkv;
+    fa.a = p->a;
+    fa.b = p->b;
+    fa.conv_w = p->conv_w;
+    fa.conv_in = p->conv_in;
+    fa.conv_out = p->conv_out;
+    fa.ssm_a = p->ssm_a;
+    fa.dt_bias = p->dt_bias;
+    fa.rec = rec;
+    fa.n = p->n;
+    fa.nc = nc;
+    fa.qkv_stride = p->qkv_stride;
+    fa.zab_stride = p->zab_stride;
+    // Map over the q / k / v part of the projection rows (for the L2 prefetch of each chunk's
+    // rows): 128 channels x 67 rows per box (a chunk and the three rows before it).
+    CUtensorMap qkvmap;
+    {
+      const cuuint64_t dims[2] = {8192, p->n};
+      const cuuint64_t strides[1] = {uint64_t(p->qkv_stride) * 4};
+      const cuuint32_t box[2] = {128, 67};
+      if ((st = f32_map(&qkvmap, p->qkv, dims, strides, box)) != MISO_OK)
+        return st;
+    }
+    pf::front_kernel<<<dim3(nc, pf::kKHeads), pf::kFrontThreads, pf::kFrontSmemBytes, s>>>(
+        qkvmap, fa);
     if ((st = launch_status()) != MISO_OK)
       return st;
   }
   if (stages & 2) {
-    ra.c_begin = 0;
-    ra.c_end = nc;
-    dc::recur_kernel<<<32, dc::kRecurThreads, dc::kRecurSmemBytes, s>>>(
-        wmap, qgmap, ksmap, vmap, vlmap, tumap, aqkmap, aqklmap, ra);
+    CUtensorMap qghmap, qglmap, wmap, umap, bhmap, blmap;
+    {
+      const cuuint64_t dims[2] = {128, uint64_t(32) * nc * 64};
+      const cuuint64_t strides[1] = {128 * 2};
+      const cuuint32_t box[2] = {64, 64};
+      if ((st = f16_map(&qghmap, rec.qgh, 2, dims, strides, box)) != MISO_OK ||
+          (st = f16_map(&qglmap, rec.qgl, 2, dims, strides, box)) != MISO_OK ||
+          (st = f16_map(&wmap, rec.w, 2, dims, strides, box)) != MISO_OK)
+        return st;
+    }
+    {
+      const cuuint64_t dims[2] = {128, uint64_t(32) * nc * 64};
+      const cuuint64_t strides[1] = {128 * 4};
+      const cuuint32_t box[2] = {32, 64};
+      if ((st = f32_map(&umap, rec.u, dims, strides, box)) != MISO_OK)
+        return st;
+    }
+    {
+      const cuuint64_t dims[2] = {64, uint64_t(32) * nc * 192};
+      const cuuint64_t strides[1] = {64 * 2};
+      const cuuint32_t box[2] = {64, 192};
+      if ((st = f16_map(&bhmap, rec.bh, 2, dims, strides, box)) != MISO_OK ||
+          (st = f16_map(&blmap, rec.bl, 2, dims, strides, box)) != MISO_OK)
+        return st;
+    }
+    pf::ChainArgs ca;
+    ca.egl = rec.egl;
+    ca.state = p->state;
+    ca.out = p->out;
+    ca.n = p->n;
+    ca.nc = nc;
+    pf::chain_kernel<<<pf::kVHeads, pf::kChainThreads, pf::kChainSmemBytes, s>>>(
+        qghmap, qglmap, wmap, umap, bhmap, blmap, ca);
+    if ((st = launch_status()) != MISO_OK)
+      return st;
+    pf::GateArgs ga;
+    ga.out = p->out;
+    ga.z = p->z;
+    ga.norm_w = p->norm_w;
+    ga.n = p->n;
+    ga.zab_stride = p->zab_stride;
+    ga.eps = p->eps;
+    const unsigned rows = p->n * pf::kVHeads, per_block = pf::kGateThreads / 32;
+    const unsigned blocks = (rows + per_block - 1) / per_block;
+    pf::gate_kernel<<<blocks < 8u * d->sms ? blocks : 8u * d->sms, pf::kGateThreads, 0, s>>>(ga);
     return launch_status();
   }
   return MISO_OK;
