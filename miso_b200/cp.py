@@ -3,10 +3,12 @@
 Attention (the gated GQA layer): zig-zag partition of the T tokens into 2W chunks of T / 2W; rank
 r owns chunks r and 2W - 1 - r, which balances the causal work (chunk i costs ~ i + 1/2). Each
 rank runs the prep (norms, RoPE, fp16 KV append) of its own tokens into a full-length KV cache,
-the ranks exchange their KV chunks (the only collective of the attention layer; every rank ends
-up holding the whole cache, which the decode phase then reuses), and each rank runs the causal
-tensor-core prefill of its two query chunks against all keys before them
-(miso_attn_prefill_tc with pos0 = chunk start).
+then the ranks pass their chunk pairs around a ring (W - 1 steps of NCCL send / receive over
+NVLink, the only collective of the attention layer; every rank ends up holding the whole cache,
+which the decode phase then reuses). The low chunk r needs only the keys of chunks 0..r, i.e. of
+ranks 0..r, which have arrived after ring step r: its causal tensor-core prefill
+(miso_attn_prefill_tc with pos0 = chunk start) starts then, while the remaining steps are still
+in flight; the high chunk 2W - 1 - r needs every rank's keys and follows the last step.
 
 Gated DeltaNet layers: the recurrence needs the state at the end of the previous tokens, so the
 sequence is cut into W contiguous segments and the state is handed from rank r - 1 to rank r.
@@ -17,8 +19,8 @@ recurrences alone. Independent layers form a wavefront: rank r runs layer l's re
 rank r + 1 runs layer l - 1's, so L layers take (W + L - 1) recurrence times.
 
 The orchestration is written against small callables (compute a segment, send / receive a state,
-all-gather a chunk) so that the same code runs over NCCL with the CUDA kernels and over gloo with
-the CPU oracle in the tests.
+one ring step of KV chunks) so that the same code runs over NCCL with the CUDA kernels and over
+gloo with the CPU oracle in the tests.
 """
 from __future__ import annotations
 
@@ -55,27 +57,37 @@ class AttentionCp:
     """One rank's share of the context-parallel attention prefill.
 
     prep(start, n)        prep of tokens [start, start + n) into the local full-length cache
-    gather(chunk_index)   makes zig-zag chunk `chunk_index` of every rank present in the local
-                          cache (all-gather of that chunk's K / V over the ranks)
-    attend(start, n)      causal prefill of query tokens [start, start + n) against keys [0, start + n)
+    ring_step(k)          ring step k = 1 .. W - 1: send to rank + 1 the two chunks of rank
+                          (rank - k + 1) mod W (this rank's own at k = 1, then those received at
+                          step k - 1) and receive from rank - 1 those of rank (rank - k) mod W
+                          into the local cache
+    attend(start, n)      causal prefill of query tokens [start, start + n) against the keys
+                          [0, start + n)
     """
     t: int
     world: int
     rank: int
     prep: Callable[[int, int], None]
-    gather: Callable[[int], None]
+    ring_step: Callable[[int], None]
     attend: Callable[[int, int], None]
 
     def run(self) -> None:
-        mine = zigzag_chunks(self.t, self.world, self.rank)
-        for start, n in mine:
-            self.prep(start, n)
-        # Chunk slot 0 (positions r s) and slot 1 (positions (2W - 1 - r) s) of every rank; every
-        # rank takes part in both all-gathers in the same order.
-        for slot in range(2):
-            self.gather(slot)
-        for start, n in mine:
-            self.attend(start, n)
+        low, high = zigzag_chunks(self.t, self.world, self.rank)
+        self.prep(*low)
+        self.prep(*high)
+        # After step k this rank holds the chunks of ranks rank, rank - 1, ..., rank - k.
+        if self.rank == 0:
+            self.attend(*low)
+        for k in range(1, self.world):
+            self.ring_step(k)
+            if k == self.rank:
+                self.attend(*low)
+        self.attend(*high)
+
+
+def ring_sources(world: int, rank: int, k: int) -> tuple[int, int]:
+    """(rank whose chunks this rank forwards, rank whose chunks it receives) at ring step k."""
+    return (rank - k + 1) % world, (rank - k) % world
 
 
 @dataclass
@@ -193,7 +205,9 @@ DN_PROJ = 12352    # [qkv 8192 | z 4096 | a 32 | b 32] per token
 class GpuAttentionCp:
     """Buffers and kernels of one rank's context-parallel attention prefill over a projection
     buffer proj [t][9216] (the rank reads only its own rows). After run(), self.k / self.v hold
-    the whole [2][t][256] fp16 cache on every rank and self.core [t][16][256] the rank's rows."""
+    the whole [2][t][256] fp16 cache on every rank and self.core [t][16][256] the rank's rows.
+    The ring runs on its own stream; `stream` (the compute stream) waits for a step only where
+    an attention launch needs that step's keys."""
 
     def __init__(self, t: int, world: int, rank: int, proj, q_norm, k_norm, inv_freq,
                  eps: float, stream, group=None):
@@ -208,7 +222,9 @@ class GpuAttentionCp:
         self.v = torch.zeros_like(self.k)
         self.q16 = torch.empty((t, 16, 256), dtype=torch.float16, device=dev)
         self.core = torch.empty((t, 16, 256), dtype=torch.float32, device=dev)
-        self.cp = AttentionCp(t, world, rank, self._prep, self._gather, self._attend)
+        self.ring_stream = torch.cuda.Stream(device=dev, priority=-100) if world > 1 else None
+        self.prepped = torch.cuda.Event()
+        self.cp = AttentionCp(t, world, rank, self._prep, self._ring_step, self._attend)
 
     def _prep(self, start: int, n: int) -> None:
         import ctypes
@@ -221,18 +237,29 @@ class GpuAttentionCp:
         bp = capi.AttnPrepBatchParams(tok0, n, ATTN_PROJ)
         capi.check("miso_attn_prep_batch_f16", self.lib.miso_attn_prep_batch_f16(
             ctypes.byref(bp), self.q16.data_ptr() + start * 16 * 256 * 2, self.stream.cuda_stream))
+        self.prepped.record(self.stream)  # after the second prep: both own chunks are in place
 
-    def _gather(self, slot: int) -> None:
+    def _ring_step(self, k: int) -> None:
+        import torch
         import torch.distributed as dist
-        if self.world == 1:
-            return
-        starts = [zigzag_chunks(self.t, self.world, r)[slot][0] for r in range(self.world)]
+        if k == 1:  # the own chunks are sent once prepped (not after any attention queued since)
+            self.ring_stream.wait_event(self.prepped)
+        fwd, src = ring_sources(self.world, self.rank, k)
         s = self.t // (2 * self.world)
-        mine = starts[self.rank]
-        for cache in (self.k, self.v):
-            for h in range(2):
-                dist.all_gather([cache[h, st:st + s] for st in starts], cache[h, mine:mine + s],
-                                group=self.group)
+        nxt, prv = (self.rank + 1) % self.world, (self.rank - 1) % self.world
+        ops = []
+        with torch.cuda.stream(self.ring_stream):
+            for (fs, _), (rs, _) in zip(zigzag_chunks(self.t, self.world, fwd),
+                                        zigzag_chunks(self.t, self.world, src)):
+                for cache in (self.k, self.v):
+                    for h in range(2):
+                        ops.append(dist.P2POp(dist.isend, cache[h, fs:fs + s], nxt, self.group))
+                        ops.append(dist.P2POp(dist.irecv, cache[h, rs:rs + s], prv, self.group))
+            for w in dist.batch_isend_irecv(ops):
+                w.wait()  # orders the ring stream after the transfers
+        done = torch.cuda.Event()
+        done.record(self.ring_stream)
+        self.stream.wait_event(done)  # only attention launched after this step waits for it
 
     def _attend(self, start: int, n: int) -> None:
         import ctypes

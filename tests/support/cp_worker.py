@@ -34,16 +34,19 @@ def attention_case(rank: int, world: int) -> None:
         k_loc[:, start:start + n] = torch.from_numpy(k_full[:, start:start + n])
         v_loc[:, start:start + n] = torch.from_numpy(v_full[:, start:start + n])
 
-    def gather(slot):
-        starts = [cp.zigzag_chunks(t, world, r)[slot][0] for r in range(world)]
+    def ring_step(k):
+        fwd, src = cp.ring_sources(world, rank, k)
         s = t // (2 * world)
-        mine = starts[rank]
-        for cache in (k_loc, v_loc):
-            for h in range(2):
-                parts = [torch.empty((s, 256), dtype=torch.float16) for _ in range(world)]
-                dist.all_gather(parts, cache[h, mine:mine + s].contiguous())
-                for st, part in zip(starts, parts):
-                    cache[h, st:st + s] = part
+        nxt, prv = (rank + 1) % world, (rank - 1) % world
+        for (fs, _), (rs, _) in zip(cp.zigzag_chunks(t, world, fwd),
+                                    cp.zigzag_chunks(t, world, src)):
+            for cache in (k_loc, v_loc):
+                for h in range(2):
+                    req = dist.isend(cache[h, fs:fs + s].contiguous(), nxt)
+                    buf = torch.empty((s, 256), dtype=torch.float16)
+                    dist.recv(buf, prv)
+                    req.wait()
+                    cache[h, rs:rs + s] = buf
 
     def attend(start, n):
         kb = k_loc.numpy().view(np.uint16)
@@ -51,7 +54,7 @@ def attention_case(rank: int, world: int) -> None:
         out[start:start + n] = oracle.attn_prefill(n, start, q[start:start + n],
                                                    qg[start:start + n], 8192, kb, vb, t)
 
-    cp.AttentionCp(t, world, rank, prep, gather, attend).run()
+    cp.AttentionCp(t, world, rank, prep, ring_step, attend).run()
     # Every rank now holds the whole cache.
     assert np.array_equal(k_loc.numpy(), k_full) and np.array_equal(v_loc.numpy(), v_full)
     total = torch.from_numpy(out)
@@ -163,7 +166,8 @@ def deltanet_affine_case(rank: int, world: int) -> None:
 
     def final(layer, start, n, s):
         state = s.copy()
-        out[layer][start:start + n] = run_segment(layer, start, n, ins[layer]["qkv"][start:start + n],
+        out[layer][start:start + n] = run_segment(layer, start, n,
+                                                  ins[layer]["qkv"][start:start + n],
                                                   halo[layer].copy(), state)
         final_state[layer] = state
 

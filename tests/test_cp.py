@@ -1,6 +1,6 @@
 """Context-parallel prefill (miso_b200.cp): the partition arithmetic, and the multi-rank
 orchestration run as gloo ranks on the CPU with the oracle in place of the kernels (attention:
-zig-zag chunks + KV all-gather; DeltaNet: state hand-off wavefront), bit-exact against a
+zig-zag chunks + ring KV exchange; DeltaNet: state hand-off wavefront), bit-exact against a
 single-process run."""
 import os
 import socket
@@ -76,6 +76,37 @@ def test_deltanet_wavefront_gloo(world):
 def test_deltanet_affine_schedule_gloo(world):
     """Per-segment affine maps, all-gathered and composed, give the sequential recurrence."""
     run_ranks("deltanet_affine", world)
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_attention_ring_schedule(world):
+    """Per rank: prep of both own chunks, then W - 1 ring steps; the low chunk r is attended
+    right after step r (rank 0 before the ring), when the keys of ranks 0..r are present, and
+    the high chunk after the last step. The chunks each step forwards are those received at the
+    step before, so after step k a rank holds the chunks of ranks rank, rank - 1, ..., rank - k."""
+    t = 64 * world
+    for rank in range(world):
+        calls = []
+        rec = lambda name: (lambda *a: calls.append((name,) + a))  # noqa: E731
+        cp.AttentionCp(t, world, rank, rec("prep"), rec("ring"), rec("attend")).run()
+        low, high = cp.zigzag_chunks(t, world, rank)
+        expect = [("prep",) + low, ("prep",) + high]
+        if rank == 0:
+            expect.append(("attend",) + low)
+        for k in range(1, world):
+            expect.append(("ring", k))
+            if k == rank:
+                expect.append(("attend",) + low)
+        expect.append(("attend",) + high)
+        assert calls == expect
+        held = {rank}
+        for k in range(1, world):
+            fwd, src = cp.ring_sources(world, rank, k)
+            assert fwd in held  # forwards what it already holds
+            held.add(src)
+            if k == rank:  # the low chunk's keys: chunks 0..rank, owned by ranks 0..rank
+                assert set(range(rank + 1)) <= held
+        assert held == set(range(world))
 
 
 @pytest.mark.parametrize("world", [1, 2, 4])
