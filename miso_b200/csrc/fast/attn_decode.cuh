@@ -382,17 +382,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         dev::named_bar_sync(1, kConsumers);
-        // Outputs: thread tid takes dimension tid of every head; the loads of different partials
-        // are independent, so several are in flight at once.
-        for (unsigned h = 0; h < kGroup; ++h) {
-          const unsigned i = h * kDim + tid;
-          float ov = 0.0f;
+        // Outputs: thread tid takes dimension tid of every head (eight independent sums, each
+        // in partial order), so 8 x 4 loads are in flight at once.
+        float ov[kGroup];
+#pragma unroll
+        for (unsigned h = 0; h < kGroup; ++h)
+          ov[h] = 0.0f;
 #pragma unroll 4
-          for (unsigned k = 0; k < np; ++k)
-            if (const float* pp = part_of(k))
-              ov += wts[k * kGroup + h] * __ldcg(pp + 2 * kGroup + i);
-          out[i] = ov / Ls[h] / (1.0f + fast_exp(-gate[h * 2 * kDim + tid]));
-        }
+        for (unsigned k = 0; k < np; ++k)
+          if (const float* pp = part_of(k)) {
+#pragma unroll
+            for (unsigned h = 0; h < kGroup; ++h)
+              ov[h] += wts[k * kGroup + h] * __ldcg(pp + 2 * kGroup + h * kDim + tid);
+          }
+#pragma unroll
+        for (unsigned h = 0; h < kGroup; ++h)
+          out[h * kDim + tid] = ov[h] / Ls[h] / (1.0f + fast_exp(-gate[h * 2 * kDim + tid]));
         if (tid == 0)
           a.counters[seg] = 0;  // ready for the next call
       }
