@@ -49,7 +49,8 @@ enum {
 
 /* Device status word (miso_device_status): the first failure recorded on the device. Low byte:
  * MISO_STATUS_*; bits 8 and up: the kernel wait site that recorded it (0x11-0x13 batched decode,
- * 0x20-0x21 tensor-core prefill, 0x30-0x31 tensor-core DeltaNet prefill). */
+ * 0x14 batched DeltaNet step, 0x20-0x21 tensor-core prefill, 0x30-0x31 tensor-core DeltaNet
+ * prefill). */
 enum { MISO_STATUS_OK = 0, MISO_STATUS_TIMEOUT = 1 };
 
 /* ---------------------------------------------------------------------------------------------

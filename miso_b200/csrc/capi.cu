@@ -117,6 +117,10 @@ int device_info(DeviceInfo** out) {
                                cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(miso::fast::prefill::kSmemBytes));
     if (a == cudaSuccess)
+      a = cudaFuncSetAttribute(miso::fast::dnstep::step_batched_kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(miso::fast::dnstep::kSmemBytes));
+    if (a == cudaSuccess)
       a = cudaFuncSetAttribute(miso::fast::dnpf::front_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(miso::fast::dnpf::kFrontSmemBytes));
@@ -527,7 +531,7 @@ int miso_deltanet_step_batched(const miso_deltanet_step_batched_params* p, void*
       p->norm_w == nullptr || p->conv_in == nullptr || p->conv_out == nullptr ||
       p->conv_in == p->conv_out || p->state == nullptr || p->out == nullptr || p->batch == 0 ||
       p->batch > 65535 || !aligned16(p->state) || !aligned16(p->out) ||
-      !aligned16(p->norm_w))
+      !aligned16(p->norm_w) || !aligned16(p->conv_w))
     return MISO_ERR_INVALID;
   namespace ds = miso::fast::dnstep;
   ds::Args a;
@@ -546,7 +550,14 @@ int miso_deltanet_step_batched(const miso_deltanet_step_batched_params* p, void*
   a.batch = p->batch;
   a.in_stride = p->in_stride;
   a.eps = p->eps;
-  ds::step_batched_kernel<<<dim3(ds::kVHeads, p->batch), ds::kThreads, 0, as_stream(stream)>>>(a);
+  DeviceInfo* d = nullptr;
+  const int st = device_info(&d);
+  if (st != MISO_OK)
+    return st;
+  const unsigned units = p->batch * ds::kVHeads;
+  const unsigned slots = unsigned(d->sms) * ds::kCtasPerSm;
+  const unsigned ctas = units < slots ? units : slots;
+  ds::step_batched_kernel<<<ctas, ds::kThreads, ds::kSmemBytes, as_stream(stream)>>>(a);
   return launch_status();
 }
 

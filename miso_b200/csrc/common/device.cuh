@@ -109,6 +109,17 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 
 // ---- TMA --------------------------------------------------------------------------------------
 
+// Untiled bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from global to
+// shared memory, completion signalled on `bar` (complete_tx).
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
+                                          uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
