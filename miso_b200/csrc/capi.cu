@@ -86,6 +86,61 @@ struct DeviceInfo {
 
 DeviceInfo g_dev[kMaxDevices];
 
+// Streams and events of the pipelined DeltaNet prefill (one set per device, created on first use):
+// the per-piece front launches, chain launches and gate launches run on three streams that fork
+// from and join back into the caller's stream. The mutex keeps one call's enqueue sequence whole
+// (the events are reused from call to call).
+constexpr int kDnMaxPieces = 64;
+constexpr unsigned kDnPieceChunks = 16;  // chunks of 64 tokens per piece
+struct DnPipe {
+  std::once_flag once;
+  int status = MISO_OK;
+  std::mutex mu;
+  cudaStream_t front = nullptr, chain = nullptr, gate = nullptr;
+  cudaEvent_t fork = nullptr, front_done[kDnMaxPieces] = {}, chain_done[kDnMaxPieces] = {};
+  cudaEvent_t join_front = nullptr, join_gate = nullptr;
+};
+DnPipe g_dn_pipe[kMaxDevices];
+
+int dn_pipe(DnPipe** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess)
+    return static_cast<int>(e);
+  if (dev < 0 || dev >= kMaxDevices)
+    return MISO_ERR_NO_DEVICE;
+  DnPipe& q = g_dn_pipe[dev];
+  std::call_once(q.once, [&] {
+    int lo = 0, hi = 0;
+    cudaError_t r = cudaDeviceGetStreamPriorityRange(&lo, &hi);
+    // The chain (the critical path) at the highest priority, so that its CTAs are placed before
+    // waiting front and gate CTAs whenever an SM frees up.
+    if (r == cudaSuccess)
+      r = cudaStreamCreateWithPriority(&q.chain, cudaStreamNonBlocking, hi);
+    if (r == cudaSuccess)
+      r = cudaStreamCreateWithPriority(&q.front, cudaStreamNonBlocking, lo);
+    if (r == cudaSuccess)
+      r = cudaStreamCreateWithPriority(&q.gate, cudaStreamNonBlocking, lo);
+    const unsigned fl = cudaEventDisableTiming;
+    if (r == cudaSuccess)
+      r = cudaEventCreateWithFlags(&q.fork, fl);
+    if (r == cudaSuccess)
+      r = cudaEventCreateWithFlags(&q.join_front, fl);
+    if (r == cudaSuccess)
+      r = cudaEventCreateWithFlags(&q.join_gate, fl);
+    for (int i = 0; r == cudaSuccess && i < kDnMaxPieces; ++i) {
+      r = cudaEventCreateWithFlags(&q.front_done[i], fl);
+      if (r == cudaSuccess)
+        r = cudaEventCreateWithFlags(&q.chain_done[i], fl);
+    }
+    q.status = r == cudaSuccess ? MISO_OK : static_cast<int>(r);
+  });
+  if (q.status != MISO_OK)
+    return q.status;
+  *out = &q;
+  return MISO_OK;
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::once_flag g_encode_once;
 
@@ -171,13 +226,14 @@ int f16_map(CUtensorMap* map, const void* ptr, cuuint32_t rank, const cuuint64_t
   return r == CUDA_SUCCESS ? MISO_OK : MISO_ERR_INVALID;
 }
 
-// 2-D fp32 tensor map without swizzle; dims / box innermost first, row stride in bytes.
+// 2-D fp32 tensor map, by default without swizzle; dims / box innermost first, row stride in
+// bytes.
 int f32_map(CUtensorMap* map, const void* ptr, const cuuint64_t* dims, const cuuint64_t* strides,
-            const cuuint32_t* box) {
+            const cuuint32_t* box, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE) {
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(ptr),
-                              dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                              CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? MISO_OK : MISO_ERR_INVALID;
 }
@@ -530,8 +586,10 @@ int miso_deltanet_step_batched(const miso_deltanet_step_batched_params* p, void*
       p->b == nullptr || p->conv_w == nullptr || p->ssm_a == nullptr || p->dt_bias == nullptr ||
       p->norm_w == nullptr || p->conv_in == nullptr || p->conv_out == nullptr ||
       p->conv_in == p->conv_out || p->state == nullptr || p->out == nullptr || p->batch == 0 ||
-      p->batch > 65535 || !aligned16(p->state) || !aligned16(p->out) ||
-      !aligned16(p->norm_w) || !aligned16(p->conv_w))
+      p->batch > 65535 || p->in_stride < 8192 || p->in_stride % 4 != 0 ||
+      !aligned16(p->qkv) || !aligned16(p->z) || !aligned16(p->a) || !aligned16(p->b) ||
+      !aligned16(p->state) || !aligned16(p->out) ||
+      !aligned16(p->norm_w) || !aligned16(p->conv_w) || !aligned16(p->conv_in))
     return MISO_ERR_INVALID;
   namespace ds = miso::fast::dnstep;
   ds::Args a;
@@ -551,13 +609,24 @@ int miso_deltanet_step_batched(const miso_deltanet_step_batched_params* p, void*
   a.in_stride = p->in_stride;
   a.eps = p->eps;
   DeviceInfo* d = nullptr;
-  const int st = device_info(&d);
+  int st = device_info(&d);
   if (st != MISO_OK)
     return st;
+  if ((st = tensor_map_encoder()) != MISO_OK)
+    return st;
+  // The states as [batch x 32 x 128 rows k][128 v] fp32, loaded as four [128][32] boxes per unit.
+  CUtensorMap smap;
+  {
+    const cuuint64_t dims[2] = {128, uint64_t(p->batch) * ds::kVHeads * 128};
+    const cuuint64_t strides[1] = {128 * 4};
+    const cuuint32_t box[2] = {32, 128};
+    if ((st = f32_map(&smap, p->state, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) != MISO_OK)
+      return st;
+  }
   const unsigned units = p->batch * ds::kVHeads;
   const unsigned slots = unsigned(d->sms) * ds::kCtasPerSm;
   const unsigned ctas = units < slots ? units : slots;
-  ds::step_batched_kernel<<<ctas, ds::kThreads, ds::kSmemBytes, as_stream(stream)>>>(a);
+  ds::step_batched_kernel<<<ctas, ds::kThreads, ds::kSmemBytes, as_stream(stream)>>>(smap, a);
   return launch_status();
 }
 
@@ -630,8 +699,9 @@ int dn_prefill_tc(const miso_deltanet_seq_params* p, void* scratch, size_t scrat
   rec.egl = reinterpret_cast<float*>(base + L.egl);
   cudaStream_t s = as_stream(stream);
 
+  pf::FrontArgs fa;
+  CUtensorMap qkvmap;
   if (stages & 1) {
-    pf::FrontArgs fa;
     fa.qkv = p->qkv;
     fa.a = p->a;
     fa.b = p->b;
@@ -645,23 +715,20 @@ int dn_prefill_tc(const miso_deltanet_seq_params* p, void* scratch, size_t scrat
     fa.nc = nc;
     fa.qkv_stride = p->qkv_stride;
     fa.zab_stride = p->zab_stride;
+    fa.c0 = 0;
+    fa.ahead = unsigned(d->sms);
     // Map over the q / k / v part of the projection rows (for the L2 prefetch of each chunk's
     // rows): 128 channels x 67 rows per box (a chunk and the three rows before it).
-    CUtensorMap qkvmap;
-    {
-      const cuuint64_t dims[2] = {8192, p->n};
-      const cuuint64_t strides[1] = {uint64_t(p->qkv_stride) * 4};
-      const cuuint32_t box[2] = {128, 67};
-      if ((st = f32_map(&qkvmap, p->qkv, dims, strides, box)) != MISO_OK)
-        return st;
-    }
-    pf::front_kernel<<<dim3(nc, pf::kKHeads), pf::kFrontThreads, pf::kFrontSmemBytes, s>>>(
-        qkvmap, fa);
-    if ((st = launch_status()) != MISO_OK)
+    const cuuint64_t dims[2] = {8192, p->n};
+    const cuuint64_t strides[1] = {uint64_t(p->qkv_stride) * 4};
+    const cuuint32_t box[2] = {128, 67};
+    if ((st = f32_map(&qkvmap, p->qkv, dims, strides, box)) != MISO_OK)
       return st;
   }
+  CUtensorMap qghmap, qglmap, wmap, umap, bhmap, blmap;
+  pf::ChainArgs ca;
+  pf::GateArgs ga;
   if (stages & 2) {
-    CUtensorMap qghmap, qglmap, wmap, umap, bhmap, blmap;
     {
       const cuuint64_t dims[2] = {128, uint64_t(32) * nc * 64};
       const cuuint64_t strides[1] = {128 * 2};
@@ -686,28 +753,87 @@ int dn_prefill_tc(const miso_deltanet_seq_params* p, void* scratch, size_t scrat
           (st = f16_map(&blmap, rec.bl, 2, dims, strides, box)) != MISO_OK)
         return st;
     }
-    pf::ChainArgs ca;
     ca.egl = rec.egl;
     ca.state = p->state;
     ca.out = p->out;
     ca.n = p->n;
     ca.nc = nc;
-    pf::chain_kernel<<<pf::kVHeads, pf::kChainThreads, pf::kChainSmemBytes, s>>>(
-        qghmap, qglmap, wmap, umap, bhmap, blmap, ca);
-    if ((st = launch_status()) != MISO_OK)
-      return st;
-    pf::GateArgs ga;
     ga.out = p->out;
     ga.z = p->z;
     ga.norm_w = p->norm_w;
-    ga.n = p->n;
     ga.zab_stride = p->zab_stride;
     ga.eps = p->eps;
-    const unsigned rows = p->n * pf::kVHeads, per_block = pf::kGateThreads / 32;
-    const unsigned blocks = (rows + per_block - 1) / per_block;
-    pf::gate_kernel<<<blocks < 8u * d->sms ? blocks : 8u * d->sms, pf::kGateThreads, 0, s>>>(ga);
-    return launch_status();
   }
+  // Chunks [c0, c0 + cnt) of each stage.
+  auto front = [&](cudaStream_t q, unsigned c0, unsigned cnt) {
+    pf::FrontArgs f = fa;
+    f.c0 = c0;
+    pf::front_kernel<<<dim3(cnt, pf::kKHeads), pf::kFrontThreads, pf::kFrontSmemBytes, q>>>(
+        qkvmap, f);
+    return launch_status();
+  };
+  auto chain = [&](cudaStream_t q, unsigned c0, unsigned cnt) {
+    pf::ChainArgs c = ca;
+    c.c0 = c0;
+    c.cnt = cnt;
+    pf::chain_kernel<<<pf::kVHeads, pf::kChainThreads, pf::kChainSmemBytes, q>>>(
+        qghmap, qglmap, wmap, umap, bhmap, blmap, c);
+    return launch_status();
+  };
+  auto gate = [&](cudaStream_t q, unsigned c0, unsigned cnt) {
+    pf::GateArgs g = ga;
+    g.t0 = c0 * 64;
+    g.n = (c0 + cnt) * 64 < p->n ? (c0 + cnt) * 64 : p->n;
+    const unsigned rows = (g.n - g.t0) * pf::kVHeads, per_block = pf::kGateThreads / 32;
+    const unsigned blocks = (rows + per_block - 1) / per_block;
+    pf::gate_kernel<<<blocks < 8u * d->sms ? blocks : 8u * d->sms, pf::kGateThreads, 0, q>>>(g);
+    return launch_status();
+  };
+
+  if (stages != 3 || nc <= kDnPieceChunks) {
+    if ((stages & 1) && (st = front(s, 0, nc)) != MISO_OK)
+      return st;
+    if ((stages & 2) && ((st = chain(s, 0, nc)) != MISO_OK || (st = gate(s, 0, nc)) != MISO_OK))
+      return st;
+    return MISO_OK;
+  }
+
+  // Pipelined: the sequence in pieces of chunks; the front of piece k + 1 runs on the SMs the
+  // chain of piece k leaves free (the chain uses one SM per V head), and the gate of piece k
+  // overlaps both. Piece k's chain waits for its front and for piece k - 1's chain (stream order;
+  // it carries the state), its gate for its chain.
+  DnPipe* q = nullptr;
+  if ((st = dn_pipe(&q)) != MISO_OK)
+    return st;
+  std::lock_guard<std::mutex> lock(q->mu);
+  unsigned per = kDnPieceChunks;
+  if ((nc + per - 1) / per > unsigned(kDnMaxPieces))
+    per = (nc + kDnMaxPieces - 1) / kDnMaxPieces;
+  fa.ahead = unsigned(d->sms) > unsigned(pf::kVHeads) ? unsigned(d->sms) - pf::kVHeads : 1u;
+  auto ok = [](cudaError_t e) { return e == cudaSuccess ? MISO_OK : static_cast<int>(e); };
+  if ((st = ok(cudaEventRecord(q->fork, s))) != MISO_OK ||
+      (st = ok(cudaStreamWaitEvent(q->front, q->fork, 0))) != MISO_OK ||
+      (st = ok(cudaStreamWaitEvent(q->chain, q->fork, 0))) != MISO_OK ||
+      (st = ok(cudaStreamWaitEvent(q->gate, q->fork, 0))) != MISO_OK)
+    return st;
+  for (unsigned k = 0, c0 = 0; c0 < nc; ++k, c0 += per) {
+    const unsigned cnt = nc - c0 < per ? nc - c0 : per;
+    if ((st = front(q->front, c0, cnt)) != MISO_OK ||
+        (st = ok(cudaEventRecord(q->front_done[k], q->front))) != MISO_OK ||
+        (st = ok(cudaStreamWaitEvent(q->chain, q->front_done[k], 0))) != MISO_OK ||
+        (st = chain(q->chain, c0, cnt)) != MISO_OK ||
+        (st = ok(cudaEventRecord(q->chain_done[k], q->chain))) != MISO_OK ||
+        (st = ok(cudaStreamWaitEvent(q->gate, q->chain_done[k], 0))) != MISO_OK ||
+        (st = gate(q->gate, c0, cnt)) != MISO_OK)
+      return st;
+  }
+  // Join: the caller's stream continues after the last gate (which follows every chain) and the
+  // last front.
+  if ((st = ok(cudaEventRecord(q->join_front, q->front))) != MISO_OK ||
+      (st = ok(cudaEventRecord(q->join_gate, q->gate))) != MISO_OK ||
+      (st = ok(cudaStreamWaitEvent(s, q->join_front, 0))) != MISO_OK ||
+      (st = ok(cudaStreamWaitEvent(s, q->join_gate, 0))) != MISO_OK)
+    return st;
   return MISO_OK;
 }
 

@@ -126,6 +126,8 @@ struct FrontArgs {
   const float* dt_bias;
   Records rec;
   unsigned n, nc, qkv_stride, zab_stride;
+  unsigned c0;     // chunk of blockIdx.x = 0 (the launch covers chunks [c0, c0 + gridDim.x))
+  unsigned ahead;  // CTAs resident at a time: the unit `ahead` places later is prefetched
 };
 
 constexpr int kFrontThreads = 512;  // 16 warps: 4 tokens each in the convs
@@ -236,7 +238,7 @@ __global__ void __launch_bounds__(kFrontThreads, 1)
       dev::set_status(dev::kStatusTimeout, 0x31);
     return;
   }
-  const unsigned c = blockIdx.x, kh = blockIdx.y, tid = threadIdx.x, warp = tid / 32,
+  const unsigned c = a.c0 + blockIdx.x, kh = blockIdx.y, tid = threadIdx.x, warp = tid / 32,
                  lane = tid % 32;
   const unsigned nc = a.nc;
   const uint32_t sbase = dev::smem_u32(smem);
@@ -410,6 +412,19 @@ __global__ void __launch_bounds__(kFrontThreads, 1)
 #pragma unroll
     for (int i = 0; i < kTok; ++i)
       put4(vt, kTok * warp + i, ch, kBox, yv[i], vt + 2 * kBox);
+  }
+  // This CTA's input rows have been read: bring the rows of the unit that will run `ahead` CTAs
+  // later (the next wave, roughly) into L2 while this one computes.
+  if (tid == 0) {
+    const unsigned nid = blockIdx.y * gridDim.x + blockIdx.x + a.ahead;
+    if (nid < gridDim.x * gridDim.y) {
+      const unsigned c2 = a.c0 + nid % gridDim.x, kh2 = nid / gridDim.x;
+      const int y0 = int(c2 * kC) - 3;
+      tma_prefetch_2d(&qkvmap, int(kh2 * kDim), y0);
+      tma_prefetch_2d(&qkvmap, int(kQkCh + kh2 * kDim), y0);
+      tma_prefetch_2d(&qkvmap, int(kVCh0 + kh2 * kDim), y0);
+      tma_prefetch_2d(&qkvmap, int(kVCh0 + (kh2 + kKHeads) * kDim), y0);
+    }
   }
   // The final conv history (the last three input rows) of this unit's channels.
   if (c == nc - 1) {
@@ -705,9 +720,10 @@ __global__ void __launch_bounds__(kFrontThreads, 1)
 
 struct ChainArgs {
   const float* egl;  // [32][nc] e^(g_l)
-  float* state;      // [32][128 k][128 v]
+  float* state;      // [32][128 k][128 v]: read before chunk c0, written after the last one
   float* out;        // [n][4096]: the pre-norm outputs O (gate_kernel finishes them)
   unsigned n, nc;
+  unsigned c0, cnt;  // the launch runs chunks [c0, c0 + cnt)
 };
 
 constexpr int kChainThreads = 448;  // warp 0 TMA, warp 1 MMA, 2-9 state, 10-13 output
@@ -799,7 +815,7 @@ __global__ void __launch_bounds__(kChainThreads, 1)
   }
   ChainBars& bar = *reinterpret_cast<ChainBars*>(smem + kCOffBar);
   const unsigned h = blockIdx.x, warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const unsigned nc = a.nc;
+  const unsigned nc = a.nc, cnt = a.cnt;
   const uint32_t sbase = dev::smem_u32(smem);
 
   if (threadIdx.x == 0) {
@@ -842,9 +858,10 @@ __global__ void __launch_bounds__(kChainThreads, 1)
       dev::tma_prefetch_desc(&umap);
       dev::tma_prefetch_desc(&bhmap);
       unsigned xy_issued = 0, u_issued = 0, b_issued = 0;
-      for (unsigned c = 0; c < nc; ++c) {
+      for (unsigned c = 0; c < cnt; ++c) {  // (c counts the launch's chunks)
         const unsigned s = c & 1;
-        const int row64 = int(rec_row(h, c, nc, kC)), row192 = int(rec_row(h, c, nc, 192));
+        const int row64 = int(rec_row(h, a.c0 + c, nc, kC));
+        const int row192 = int(rec_row(h, a.c0 + c, nc, 192));
         // [X | O] operands of chunk c (stage s free once chunk c - 2's products are done):
         // rows [W; Qg_hi; Qg_lo] for even chunks, [Qg_hi; W; Qg_lo] for odd ones
         if (c >= 2 && !wait_or_abort(bar, bar.xy_empty[s], ((c >> 1) & 1) ^ 1))
@@ -895,7 +912,7 @@ __global__ void __launch_bounds__(kChainThreads, 1)
       const uint32_t id_64 = dev::idesc_f16_f32(128, 64, 0, 0);
       auto kdesc = [](uint32_t addr) { return dev::sdesc_sw128(addr, 16, 1024); };
       bool ok = true;
-      for (unsigned c = 0; ok && c < nc; ++c) {
+      for (unsigned c = 0; ok && c < cnt; ++c) {
         const unsigned s = c & 1;
         const uint32_t xs = sbase + kCOffXy + s * kXyStage;
         const uint32_t ocol = s ? kColO1 : kColO0, xycol = s ? kColO1 : kColX;
@@ -963,8 +980,8 @@ __global__ void __launch_bounds__(kChainThreads, 1)
     const float* S = a.state + size_t(h) * kDim * kDim;
     const float* us = reinterpret_cast<const float*>(smem + kCOffU + q * 8192) + lane;
     bool ok = true;
-    for (unsigned c = 0; ok && c < nc; ++c) {
-      const float el = a.egl[size_t(h) * nc + c];
+    for (unsigned c = 0; ok && c < cnt; ++c) {
+      const float el = a.egl[size_t(h) * nc + a.c0 + c];
       // E0: the fp16 high copy of S^T first (the A operand the next product waits for), then,
       // reading S^T again, the low copy and S^T *= e^(g_l). 32 columns at a time.
       if (c > 0 && !warp_wait(bar, bar.s_full, (c - 1) & 1)) {
@@ -1037,7 +1054,7 @@ __global__ void __launch_bounds__(kChainThreads, 1)
       warp_arrive(bar.d_ready);
     }
     // Final state back to [k][v] (coalesced over v).
-    if (ok && warp_wait(bar, bar.s_full, (nc - 1) & 1)) {
+    if (ok && warp_wait(bar, bar.s_full, (cnt - 1) & 1)) {
       dev::tc_fence_after();
       float* So = a.state + size_t(h) * kDim * kDim;
 #pragma unroll 1
@@ -1058,7 +1075,7 @@ __global__ void __launch_bounds__(kChainThreads, 1)
     const unsigned q = warp & 3, v = 32 * q + lane;
     const uint32_t trow = tmem + ((32u * q) << 16);
     float* out_v = a.out + h * kDim + v;
-    for (unsigned c = 0; c < nc; ++c) {
+    for (unsigned c = 0; c < cnt; ++c) {
       const unsigned b = c & 1;
       if (!warp_wait(bar, bar.o_full[b], (c >> 1) & 1))
         break;
@@ -1075,7 +1092,7 @@ __global__ void __launch_bounds__(kChainThreads, 1)
       }
       dev::tc_fence_before();
       warp_arrive(bar.o_free[b]);  // O_b is in registers: release it
-      const unsigned t0 = c * kC;
+      const unsigned t0 = (a.c0 + c) * kC;
       float* dst = out_v + size_t(t0) * kVHeads * kDim;
       if (t0 + kC <= a.n) {
 #pragma unroll
@@ -1109,6 +1126,7 @@ struct GateArgs {
   const float* norm_w;  // [128]
   unsigned n, zab_stride;
   float eps;
+  unsigned t0;          // the launch covers tokens [t0, n)
 };
 
 constexpr int kGateThreads = 256;
@@ -1117,7 +1135,7 @@ __global__ void __launch_bounds__(kGateThreads) gate_kernel(GateArgs a) {
   const unsigned lane = threadIdx.x % 32;
   const unsigned rows = a.n * kVHeads;
   const float4 nw = reinterpret_cast<const float4*>(a.norm_w)[lane];
-  for (unsigned r = (blockIdx.x * kGateThreads + threadIdx.x) / 32; r < rows;
+  for (unsigned r = a.t0 * kVHeads + (blockIdx.x * kGateThreads + threadIdx.x) / 32; r < rows;
        r += gridDim.x * (kGateThreads / 32)) {
     const unsigned t = r / kVHeads, h = r % kVHeads;
     float4* o4 = reinterpret_cast<float4*>(a.out + size_t(r) * kDim) + lane;
