@@ -323,9 +323,8 @@ int miso_attn_prep_batch_f16(const miso_attn_prep_batch_params* p, uint16_t* q_f
  * in_stride = 12352 for the engine's [qkv | z | a | b] projection rows); its conv history
  * [8192][3] at conv_in / conv_out + b * 24576 (double-buffered: conv_in != conv_out), its state
  * [32][128][128] at state + b * 524288 (updated in place), its output at out + b * 4096.
- * Weights (conv_w [8192][4], ssm_a, dt_bias [32], norm_w [128]) are shared. qkv, z, a, b,
- * conv_w, conv_in, state, out and norm_w must be 16-byte aligned and in_stride a multiple of 4
- * that is at least 8192 (MISO_ERR_INVALID otherwise). */
+ * Weights (conv_w [8192][4], ssm_a, dt_bias [32], norm_w [128]) are shared. conv_w, state, out
+ * and norm_w must be 16-byte aligned and in_stride at least 8192 (MISO_ERR_INVALID otherwise). */
 typedef struct {
   const float* qkv;
   const float* z;

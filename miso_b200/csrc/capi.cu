@@ -586,10 +586,8 @@ int miso_deltanet_step_batched(const miso_deltanet_step_batched_params* p, void*
       p->b == nullptr || p->conv_w == nullptr || p->ssm_a == nullptr || p->dt_bias == nullptr ||
       p->norm_w == nullptr || p->conv_in == nullptr || p->conv_out == nullptr ||
       p->conv_in == p->conv_out || p->state == nullptr || p->out == nullptr || p->batch == 0 ||
-      p->batch > 65535 || p->in_stride < 8192 || p->in_stride % 4 != 0 ||
-      !aligned16(p->qkv) || !aligned16(p->z) || !aligned16(p->a) || !aligned16(p->b) ||
-      !aligned16(p->state) || !aligned16(p->out) ||
-      !aligned16(p->norm_w) || !aligned16(p->conv_w) || !aligned16(p->conv_in))
+      p->batch > 65535 || p->in_stride < 8192 || !aligned16(p->state) || !aligned16(p->out) ||
+      !aligned16(p->norm_w) || !aligned16(p->conv_w))
     return MISO_ERR_INVALID;
   namespace ds = miso::fast::dnstep;
   ds::Args a;
@@ -612,21 +610,10 @@ int miso_deltanet_step_batched(const miso_deltanet_step_batched_params* p, void*
   int st = device_info(&d);
   if (st != MISO_OK)
     return st;
-  if ((st = tensor_map_encoder()) != MISO_OK)
-    return st;
-  // The states as [batch x 32 x 128 rows k][128 v] fp32, loaded as four [128][32] boxes per unit.
-  CUtensorMap smap;
-  {
-    const cuuint64_t dims[2] = {128, uint64_t(p->batch) * ds::kVHeads * 128};
-    const cuuint64_t strides[1] = {128 * 4};
-    const cuuint32_t box[2] = {32, 128};
-    if ((st = f32_map(&smap, p->state, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) != MISO_OK)
-      return st;
-  }
   const unsigned units = p->batch * ds::kVHeads;
   const unsigned slots = unsigned(d->sms) * ds::kCtasPerSm;
   const unsigned ctas = units < slots ? units : slots;
-  ds::step_batched_kernel<<<ctas, ds::kThreads, ds::kSmemBytes, as_stream(stream)>>>(smap, a);
+  ds::step_batched_kernel<<<ctas, ds::kThreads, ds::kSmemBytes, as_stream(stream)>>>(a);
   return launch_status();
 }
 
@@ -717,6 +704,7 @@ int dn_prefill_tc(const miso_deltanet_seq_params* p, void* scratch, size_t scrat
     fa.zab_stride = p->zab_stride;
     fa.c0 = 0;
     fa.ahead = unsigned(d->sms);
+    fa.per = nc;
     // Map over the q / k / v part of the projection rows (for the L2 prefetch of each chunk's
     // rows): 128 channels x 67 rows per box (a chunk and the three rows before it).
     const cuuint64_t dims[2] = {8192, p->n};
@@ -810,6 +798,7 @@ int dn_prefill_tc(const miso_deltanet_seq_params* p, void* scratch, size_t scrat
   if ((nc + per - 1) / per > unsigned(kDnMaxPieces))
     per = (nc + kDnMaxPieces - 1) / kDnMaxPieces;
   fa.ahead = unsigned(d->sms) > unsigned(pf::kVHeads) ? unsigned(d->sms) - pf::kVHeads : 1u;
+  fa.per = per;
   auto ok = [](cudaError_t e) { return e == cudaSuccess ? MISO_OK : static_cast<int>(e); };
   if ((st = ok(cudaEventRecord(q->fork, s))) != MISO_OK ||
       (st = ok(cudaStreamWaitEvent(q->front, q->fork, 0))) != MISO_OK ||

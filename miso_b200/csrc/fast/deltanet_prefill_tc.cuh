@@ -128,6 +128,7 @@ struct FrontArgs {
   unsigned n, nc, qkv_stride, zab_stride;
   unsigned c0;     // chunk of blockIdx.x = 0 (the launch covers chunks [c0, c0 + gridDim.x))
   unsigned ahead;  // CTAs resident at a time: the unit `ahead` places later is prefetched
+  unsigned per;    // chunks per launch when the sequence is covered by consecutive launches
 };
 
 constexpr int kFrontThreads = 512;  // 16 warps: 4 tokens each in the convs
@@ -142,10 +143,16 @@ constexpr int kLRow = 68;  // fp32 row stride of L (16-byte aligned rows)
 //   then          per-head vectors g, beta, e^g, e^(g_l - g), beta e^g [2][64] each
 // After the solve the A operands of W and U reuse dead space: Tw at 32K (the low [K; Q] slab 0),
 // Tu high at 48K, Tu low at 128K (over L).
+// Until the convs have read them, the raw input rows (TMA boxes of [67 rows][128 channels] fp32:
+// the chunk's rows and the three before it) occupy [64K, +4 boxes): q, k, then the two v groups
+// (dead space then: the V tiles, L and T are written after the convs).
 constexpr uint32_t kFOffKQ = 0, kFOffV = 64 * 1024, kFOffL = 128 * 1024;
 constexpr int kTRow = 68;  // fp32 row stride of T (rows 64 floats apart would share banks)
 constexpr uint32_t kFOffT = kFOffL + 2 * kC * kLRow * 4;
-constexpr uint32_t kFOffVec = kFOffT + 2 * kC * kTRow * 4;
+constexpr uint32_t kRawBox = 67 * kDim * 4;  // 34304 bytes
+constexpr uint32_t kFOffRaw = 64 * 1024;
+constexpr uint32_t kFOffVec = kFOffRaw + 4 * kRawBox;
+static_assert(kFOffVec >= kFOffT + 2 * kC * kTRow * 4, "the vectors follow T");
 constexpr uint32_t kFOffBar = kFOffVec + 5 * 2 * kC * 4;
 constexpr size_t kFrontSmemBytes = kFOffBar + 64;
 constexpr uint32_t kFOffTw = 32 * 1024, kFOffTuh = 48 * 1024, kFOffTul = kFOffL;
@@ -178,47 +185,46 @@ __device__ __forceinline__ void copy_out(const uint8_t* tile, void* dst, uint32_
   }
 }
 
-// Column q of the off-diagonal block (a, b) of T = (I + L)^-1 for one head, a > b, given the
-// blocks (m, b) for b <= m < a: T_ab = -T_aa sum_{m=b}^{a-1} L_am T_mb (16 x 16 blocks). Four
-// consecutive lanes share a column: lane quarter rq forms rows [4 rq, 4 rq + 4) of the sum p,
-// the quad exchanges p by shuffles, and each lane finishes its four rows of T_ab.
-__device__ __forceinline__ void offdiag_column(const float* L, float* T, int a, int b, int q,
-                                               int rq) {
-  float p[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+// Off-diagonal blocks of T = (I + L)^-1 (16 x 16 blocks, a > b): T_ab = -T_aa P_ab with
+// P_ab = sum_{m=b}^{a-1} L_am T_mb. Thread (row r, column quarter cq) of a block forms
+// P_ab[r][4 cq, +4) from its own row of L and broadcast rows of T (phase 1, into P), then
+// T_ab[r][4 cq, +4) from its row of T_aa and broadcast rows of P (phase 2). T_aa is lower
+// triangular with zeros above the diagonal, so both sums run over all 16 terms.
+__device__ __forceinline__ void offdiag_p(const float* L, const float* T, float* P, int a, int b,
+                                          int r, int cq) {
+  float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
   for (int m = b; m < a; ++m) {
-    float tc[16];
+    const float* lr = L + (16 * a + r) * kLRow + 16 * m;
+    const float* tc = T + (16 * m) * kTRow + 16 * b + 4 * cq;
 #pragma unroll
-    for (int s = 0; s < 16; ++s)
-      tc[s] = T[(16 * m + s) * kTRow + 16 * b + q];
+    for (int s4 = 0; s4 < 4; ++s4) {
+      const float4 l4 = *reinterpret_cast<const float4*>(lr + 4 * s4);
+      const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const float* lr = L + (16 * a + 4 * rq + r) * kLRow + 16 * m;
-#pragma unroll
-      for (int s4 = 0; s4 < 4; ++s4) {
-        const float4 l4 = *reinterpret_cast<const float4*>(lr + 4 * s4);
-        p[r] += l4.x * tc[4 * s4] + l4.y * tc[4 * s4 + 1] + l4.z * tc[4 * s4 + 2] +
-                l4.w * tc[4 * s4 + 3];
+      for (int e = 0; e < 4; ++e) {
+        const float4 t4 = *reinterpret_cast<const float4*>(tc + (4 * s4 + e) * kTRow);
+        acc.x += lv[e] * t4.x, acc.y += lv[e] * t4.y, acc.z += lv[e] * t4.z, acc.w += lv[e] * t4.w;
       }
     }
   }
-  const unsigned quad = (threadIdx.x % 32) & ~3u;
-  float pa[16];
+  *reinterpret_cast<float4*>(P + r * 16 + 4 * cq) = acc;
+}
+
+__device__ __forceinline__ void offdiag_t(float* T, const float* P, int a, int b, int r, int cq) {
+  const float* tr = T + (16 * a + r) * kTRow + 16 * a;
+  float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll
-  for (int src = 0; src < 4; ++src)
+  for (int s4 = 0; s4 < 4; ++s4) {
+    const float4 t4 = *reinterpret_cast<const float4*>(tr + 4 * s4);
+    const float tv[4] = {t4.x, t4.y, t4.z, t4.w};
 #pragma unroll
-    for (int r = 0; r < 4; ++r)
-      pa[4 * src + r] = __shfl_sync(0xffffffffu, p[r], quad + src);
-#pragma unroll
-  for (int r = 0; r < 4; ++r) {
-    const int row = 4 * rq + r;
-    const float* tr = T + (16 * a + row) * kTRow + 16 * a;
-    float x = 0.0f;
-#pragma unroll
-    for (int s = 0; s < 16; ++s)
-      if (s <= row)
-        x += tr[s] * pa[s];
-    T[(16 * a + row) * kTRow + 16 * b + q] = -x;
+    for (int e = 0; e < 4; ++e) {
+      const float4 p4 = *reinterpret_cast<const float4*>(P + (4 * s4 + e) * 16 + 4 * cq);
+      acc.x += tv[e] * p4.x, acc.y += tv[e] * p4.y, acc.z += tv[e] * p4.z, acc.w += tv[e] * p4.w;
+    }
   }
+  *reinterpret_cast<float4*>(T + (16 * a + r) * kTRow + 16 * b + 4 * cq) =
+      make_float4(-acc.x, -acc.y, -acc.z, -acc.w);
 }
 
 // L2 prefetch of a 2-D box (no data lands in shared memory).
@@ -249,22 +255,43 @@ __global__ void __launch_bounds__(kFrontThreads, 1)
   float* egs = bs + 2 * kC;                               // e^g
   float* egls = egs + 2 * kC;                             // e^(g_l - g)
   float* fws = egls + 2 * kC;                             // beta e^g
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kFOffBar);  // KK^T, W / U
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2);
-  int* fail = reinterpret_cast<int*>(bars + 3);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kFOffBar);  // KK^T, W / U, raw q k, raw v
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4);
+  int* fail = reinterpret_cast<int*>(bars + 5);
 
   if (tid == 0) {
-    for (int i = 0; i < 2; ++i)
+    for (int i = 0; i < 4; ++i)
       dev::mbar_init(dev::smem_u32(&bars[i]), 1);
     *fail = 0;
     dev::mbar_init_fence();
-    // The chunk's input rows (and the three before it) of the unit's q, k and two v channel
-    // groups into L2, so that the conv loads below cost an L2 round trip, not an HBM one.
+    // The chunk's input rows (and the three before it; rows before the sequence read as zeros
+    // and are replaced by the conv history) of the unit's q and k channels, then of its two v
+    // channel groups, into shared memory.
     const int y0 = int(c * kC) - 3;
-    tma_prefetch_2d(&qkvmap, int(kh * kDim), y0);
-    tma_prefetch_2d(&qkvmap, int(kQkCh + kh * kDim), y0);
-    tma_prefetch_2d(&qkvmap, int(kVCh0 + kh * kDim), y0);
-    tma_prefetch_2d(&qkvmap, int(kVCh0 + (kh + kKHeads) * kDim), y0);
+    const uint32_t rq = dev::smem_u32(&bars[2]), rv = dev::smem_u32(&bars[3]);
+    dev::mbar_arrive_expect_tx(rq, 2 * kRawBox);
+    dev::tma_load_2d(sbase + kFOffRaw, &qkvmap, int(kh * kDim), y0, rq);
+    dev::tma_load_2d(sbase + kFOffRaw + kRawBox, &qkvmap, int(kQkCh + kh * kDim), y0, rq);
+    dev::mbar_arrive_expect_tx(rv, 2 * kRawBox);
+    dev::tma_load_2d(sbase + kFOffRaw + 2 * kRawBox, &qkvmap, int(kVCh0 + kh * kDim), y0, rv);
+    dev::tma_load_2d(sbase + kFOffRaw + 3 * kRawBox, &qkvmap,
+                     int(kVCh0 + (kh + kKHeads) * kDim), y0, rv);
+  }
+  // Warps 0 and 1: the a and b inputs of V head kh + 16 warp for the chunk's tokens 2 lane, +1,
+  // and the head's ssm_a and dt_bias, loaded now so that their latency overlaps the set-up.
+  float av[2] = {0.0f, 0.0f}, bv[2] = {0.0f, 0.0f}, sa_h = 0.0f, dt_h = 0.0f;
+  if (warp < 2) {
+    const unsigned h = kh + kKHeads * warp;
+    sa_h = a.ssm_a[h];
+    dt_h = a.dt_bias[h];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const unsigned t = c * kC + 2 * lane + e;
+      if (t < a.n) {
+        av[e] = a.a[size_t(t) * a.zab_stride + h];
+        bv[e] = a.b[size_t(t) * a.zab_stride + h];
+      }
+    }
   }
   if (warp == 0) {
     dev::tmem_alloc(dev::smem_u32(tmem_slot), 512);
@@ -277,15 +304,23 @@ __global__ void __launch_bounds__(kFrontThreads, 1)
   const unsigned t_first = c * kC + kTok * warp;  // warp's first token
 
   // ---- conv of four channels per lane for the warp's kTok tokens: y[i][e] -------------------
-  auto conv_rows = [&](unsigned ch, float (&y)[kTok][4]) {
+  // Channels ch .. ch + 3 (ch = group base + 4 lane) from the raw box at `raw` (row r = token
+  // c * 64 - 3 + r; rows before the sequence come from the conv history instead), with the
+  // channels' conv weights w (loaded ahead by load_w).
+  auto load_w = [&](unsigned ch, float4 (&w)[4]) {
     const float4* w4 = reinterpret_cast<const float4*>(a.conv_w + 4 * size_t(ch));
-    const float4 w[4] = {w4[0], w4[1], w4[2], w4[3]};
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      w[e] = w4[e];
+  };
+  auto conv_rows = [&](uint32_t raw, unsigned ch, const float4 (&w)[4], float (&y)[kTok][4]) {
+    const uint8_t* rows = smem + raw + (kTok * warp) * (kDim * 4) + 16 * lane;
     float4 h[3];
 #pragma unroll
     for (int s = 0; s < 3; ++s) {
       const int tt = int(t_first) - 3 + s;
       if (tt >= 0) {
-        h[s] = *reinterpret_cast<const float4*>(a.qkv + size_t(tt) * a.qkv_stride + ch);
+        h[s] = *reinterpret_cast<const float4*>(rows + s * (kDim * 4));
       } else {
         const int slot = tt + 3;
         h[s] = make_float4(a.conv_in[3 * ch + slot], a.conv_in[3 * (ch + 1) + slot],
@@ -295,10 +330,7 @@ __global__ void __launch_bounds__(kFrontThreads, 1)
     float4 xs[kTok];
 #pragma unroll
     for (int i = 0; i < kTok; ++i)
-      xs[i] = t_first + i < a.n
-                  ? *reinterpret_cast<const float4*>(a.qkv + size_t(t_first + i) * a.qkv_stride +
-                                                     ch)
-                  : make_float4(0.f, 0.f, 0.f, 0.f);
+      xs[i] = *reinterpret_cast<const float4*>(rows + (3 + i) * (kDim * 4));
 #pragma unroll
     for (int i = 0; i < kTok; ++i) {
       conv4(w, h[0], h[1], h[2], xs[i], y[i]);
@@ -318,33 +350,10 @@ __global__ void __launch_bounds__(kFrontThreads, 1)
     *reinterpret_cast<uint2*>(smem + lo_tile + off) = make_uint2(lo0, lo1);
   };
 
-  // ---- F1: q / k conv, L2 norms -> [K; Q] tiles; decays and betas --------------------------
-  {
-    const unsigned ch = 4 * lane;  // channels ch .. ch + 3 of the head
-    float yq[kTok][4], yk[kTok][4];
-    conv_rows(kh * kDim + ch, yq);
-    conv_rows(kQkCh + kh * kDim + ch, yk);
-#pragma unroll
-    for (int i = 0; i < kTok; ++i) {
-      float sq = yq[i][0] * yq[i][0] + yq[i][1] * yq[i][1] + yq[i][2] * yq[i][2] +
-                 yq[i][3] * yq[i][3];
-      float sk = yk[i][0] * yk[i][0] + yk[i][1] * yk[i][1] + yk[i][2] * yk[i][2] +
-                 yk[i][3] * yk[i][3];
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) {
-        sq += __shfl_xor_sync(0xffffffffu, sq, off);
-        sk += __shfl_xor_sync(0xffffffffu, sk, off);
-      }
-      const float rq = rsqrtf(sq + 1e-6f) * rsqrtf(static_cast<float>(kDim));
-      const float rk = rsqrtf(sk + 1e-6f);
-#pragma unroll
-      for (int e = 0; e < 4; ++e)
-        yq[i][e] *= rq, yk[i][e] *= rk;
-      const unsigned row = kTok * warp + i;
-      put4(kFOffKQ, row, ch, 16 * 1024, yk[i], kFOffKQ + 32 * 1024);
-      put4(kFOffKQ, row + kC, ch, 16 * 1024, yq[i], kFOffKQ + 32 * 1024);
-    }
-  }
+  // ---- F1: decays and betas (while the raw rows land); q / k conv, L2 norms -> [K; Q] tiles --
+  float4 wq[4], wk[4];  // conv weights of the lane's q and k channels
+  load_w(kh * kDim + 4 * lane, wq);
+  load_w(kQkCh + kh * kDim + 4 * lane, wk);
   if (warp < 2) {
     // In-chunk cumulative log decay and beta of V head kh + 16 warp (beta = 0, no decay past n).
     const unsigned hh = warp, h = kh + kKHeads * hh;
@@ -354,10 +363,8 @@ __global__ void __launch_bounds__(kFrontThreads, 1)
     for (int e = 0; e < 2; ++e) {
       const unsigned t = t0 + e;
       if (t < a.n) {
-        const float av = a.a[size_t(t) * a.zab_stride + h];
-        const float bv = a.b[size_t(t) * a.zab_stride + h];
-        l[e] = a.ssm_a[h] * softplus(av + a.dt_bias[h]);
-        bt[e] = 1.0f / (1.0f + __expf(-bv));
+        l[e] = sa_h * softplus(av[e] + dt_h);
+        bt[e] = 1.0f / (1.0f + __expf(-bv[e]));
       } else {
         l[e] = 0.0f, bt[e] = 0.0f;
       }
@@ -381,6 +388,34 @@ __global__ void __launch_bounds__(kFrontThreads, 1)
     if (lane == 0)
       a.rec.egl[size_t(h) * nc + c] = __expf(gl);
   }
+  if (!__all_sync(0xffffffffu, dev::mbar_wait(dev::smem_u32(&bars[2]), 0, 0x31)))
+    *fail = 1;  // (the conv then reads stale rows; the status word records the timeout)
+  {
+    const unsigned ch = 4 * lane;  // channels ch .. ch + 3 of the head
+    float yq[kTok][4], yk[kTok][4];
+    conv_rows(kFOffRaw, kh * kDim + ch, wq, yq);
+    conv_rows(kFOffRaw + kRawBox, kQkCh + kh * kDim + ch, wk, yk);
+#pragma unroll
+    for (int i = 0; i < kTok; ++i) {
+      float sq = yq[i][0] * yq[i][0] + yq[i][1] * yq[i][1] + yq[i][2] * yq[i][2] +
+                 yq[i][3] * yq[i][3];
+      float sk = yk[i][0] * yk[i][0] + yk[i][1] * yk[i][1] + yk[i][2] * yk[i][2] +
+                 yk[i][3] * yk[i][3];
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        sq += __shfl_xor_sync(0xffffffffu, sq, off);
+        sk += __shfl_xor_sync(0xffffffffu, sk, off);
+      }
+      const float rq = rsqrtf(sq + 1e-6f) * rsqrtf(static_cast<float>(kDim));
+      const float rk = rsqrtf(sk + 1e-6f);
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        yq[i][e] *= rq, yk[i][e] *= rk;
+      const unsigned row = kTok * warp + i;
+      put4(kFOffKQ, row, ch, 16 * 1024, yk[i], kFOffKQ + 32 * 1024);
+      put4(kFOffKQ, row + kC, ch, 16 * 1024, yq[i], kFOffKQ + 32 * 1024);
+    }
+  }
   dev::fence_proxy_async_smem();
   dev::tc_fence_before();
   __syncthreads();
@@ -403,11 +438,16 @@ __global__ void __launch_bounds__(kFrontThreads, 1)
   }
 
   // ---- F3 (while the MMA runs): v conv of both V heads -> V tiles ----------------------------
+  // (The V tiles overlap the raw q / k rows, which every warp has read before the F1 barrier.)
+  if (!__all_sync(0xffffffffu, dev::mbar_wait(dev::smem_u32(&bars[3]), 0, 0x31)))
+    *fail = 1;
 #pragma unroll 1
   for (unsigned hh = 0; hh < 2; ++hh) {
     const unsigned ch = 4 * lane;
     float yv[kTok][4];
-    conv_rows(kVCh0 + (kh + kKHeads * hh) * kDim + ch, yv);
+    float4 wv[4];
+    load_w(kVCh0 + (kh + kKHeads * hh) * kDim + ch, wv);
+    conv_rows(kFOffRaw + (2 + hh) * kRawBox, kVCh0 + (kh + kKHeads * hh) * kDim + ch, wv, yv);
     const uint32_t vt = kFOffV + 4 * hh * kBox;
 #pragma unroll
     for (int i = 0; i < kTok; ++i)
@@ -415,10 +455,19 @@ __global__ void __launch_bounds__(kFrontThreads, 1)
   }
   // This CTA's input rows have been read: bring the rows of the unit that will run `ahead` CTAs
   // later (the next wave, roughly) into L2 while this one computes.
+  // Units run in launch order (chunk fastest, then K head), launch after launch: the unit
+  // `ahead` places later may belong to the next launch (chunks [c0 + gridDim.x, + per)).
   if (tid == 0) {
-    const unsigned nid = blockIdx.y * gridDim.x + blockIdx.x + a.ahead;
+    unsigned nid = blockIdx.y * gridDim.x + blockIdx.x + a.ahead, c2 = nc, kh2 = 0;
     if (nid < gridDim.x * gridDim.y) {
-      const unsigned c2 = a.c0 + nid % gridDim.x, kh2 = nid / gridDim.x;
+      c2 = a.c0 + nid % gridDim.x, kh2 = nid / gridDim.x;
+    } else if (a.c0 + gridDim.x < nc) {
+      const unsigned c1 = a.c0 + gridDim.x, cnt = nc - c1 < a.per ? nc - c1 : a.per;
+      nid -= gridDim.x * gridDim.y;
+      if (nid < cnt * kKHeads)
+        c2 = c1 + nid % cnt, kh2 = nid / cnt;
+    }
+    if (c2 < nc) {
       const int y0 = int(c2 * kC) - 3;
       tma_prefetch_2d(&qkvmap, int(kh2 * kDim), y0);
       tma_prefetch_2d(&qkvmap, int(kQkCh + kh2 * kDim), y0);
@@ -440,6 +489,7 @@ __global__ void __launch_bounds__(kFrontThreads, 1)
   }
 
   // ---- F4: L and Aqk from the product -------------------------------------------------------
+  __syncthreads();  // every warp is past the v conv: L and T may overwrite the raw v rows
   const bool mma_ok = dev::mbar_wait(dev::smem_u32(&bars[0]), 0, 0x31);
   if (!mma_ok)
     *fail = 1;
@@ -598,16 +648,22 @@ __global__ void __launch_bounds__(kFrontThreads, 1)
         T[(i0 + r) * kTRow + i0 + int(q)] = t[r];
     }
     __syncthreads();
-    // Off-diagonal blocks by distance d = a - b: 3, 2 and 1 blocks per head.
+    // Off-diagonal blocks by distance d = a - b: 3, 2 and 1 blocks per head; thread (hh, block,
+    // row r, column quarter cq), whole warps active or idle. P goes through the Q rows of the
+    // high [K; Q] slab 0 (dead once Qg has been formed): [hh][block][16][16] fp32.
+    float* Ps = reinterpret_cast<float*>(smem + kFOffKQ + 8 * 1024);
 #pragma unroll 1
     for (int d = 1; d < 4; ++d) {
       const int nb = 4 - d;
-      // thread (hh, block, column q, row quarter rq): whole warps are active or idle
-      if (tid < unsigned(2 * nb * 16 * 4)) {
-        const int u = int(tid), rq = u % 4, q = (u / 4) % 16, blk = (u / 64) % nb,
-                  hh = u / (64 * nb);
-        offdiag_column(Ls + hh * kC * kLRow, Ts + hh * kC * kTRow, blk + d, blk, q, rq);
-      }
+      const int u = int(tid), cq = u % 4, r = (u / 4) % 16, blk = (u / 64) % nb,
+                hh = u / (64 * nb);
+      const bool act = tid < unsigned(2 * nb * 64);
+      float* P = Ps + (hh * nb + blk) * 256;
+      if (act)
+        offdiag_p(Ls + hh * kC * kLRow, Ts + hh * kC * kTRow, P, blk + d, blk, r, cq);
+      __syncthreads();
+      if (act)
+        offdiag_t(Ts + hh * kC * kTRow, P, blk + d, blk, r, cq);
       __syncthreads();
     }
 
@@ -713,6 +769,12 @@ __global__ void __launch_bounds__(kFrontThreads, 1)
   if (warp == 0) {
     dev::tc_fence_after();
     dev::tmem_dealloc(tmem, 512);
+  }
+  // After a timed-out wait on the raw rows, no copy may still land once the CTA has exited:
+  // wait (bounded) for both (a completed phase passes at once).
+  if (tid == 0 && *reinterpret_cast<volatile int*>(fail)) {
+    dev::mbar_wait(dev::smem_u32(&bars[2]), 0);
+    dev::mbar_wait(dev::smem_u32(&bars[3]), 0);
   }
 }
 
