@@ -563,7 +563,13 @@ DECODE_TRAFFIC_PER_ALGORITHMIC_BYTE = (257.0 + 6.3) / 256.8
 # ncu DRAM bytes (read + write) of one full-size launch (profiles/prefill_kernel_8k_ncu.md,
 # profiles/deltanet_prefill_tc_8k_ncu.md).
 PREFILL_8K_TRAFFIC = (221.3 + 101.5) * 1e6
-DN_PREFILL_8K_TRAFFIC = None  # no ncu capture of the current front / chain / gate kernels yet
+# DRAM bytes (read + write inside each launch) of the three kernels of one piece of 1024 tokens
+# (front 49.9 + 15.8 MB, chain 69.3 + 3.1 MB, gate 33.6 + 0.0 MB; ncu, caches flushed before each
+# launch), times the 8 pieces of a call at 8192 tokens.
+DN_PREFILL_8K_TRAFFIC = 8 * (49.94 + 15.80 + 69.26 + 3.08 + 33.56) * 1e6
+# DRAM bytes inside one launch of step_batched_kernel at batch 64 (ncu: read 143.9 MB, write
+# 87.6 MB; the remaining state writes leave L2 after the launch ends).
+DN_STEP_B64_TRAFFIC = (143.86 + 87.64) * 1e6
 
 
 def prefill_flops(n: int, pos0: int = 0) -> float:
@@ -700,13 +706,15 @@ def bench_deltanet_step(args, dev, stream, max_over_ranks, barrier, world) -> di
                       "states (zero-init), bf16-valued inputs; one launch per step",
             "bytes_per_step": nbytes,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"],
-                         "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "traffic": None,
+                         "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
+                         "traffic": DN_STEP_B64_TRAFFIC if B == 64 else None,
                          "kernel": "step_batched_kernel", "kernel_ms": ms,
                          "peak_source": pk["source"]},
             "gpu_launches": args.steps}
 
 
 DN_PREFILL_T = 8192
+DN_PIECES = -(-(DN_PREFILL_T // 64) // 16)  # pieces of 16 chunks per miso_deltanet_prefill_tc call
 # Algorithmic FLOPs of the chunked rule per (V head, chunk of 64): 2 (3 C d^2 + 3 C^2 d)
 # = 9.44 MFLOP (QK^T / KK^T, the UT-transform products, S updates), 32 heads x T / 64 chunks.
 DN_PREFILL_FLOPS_PER_HEAD_CHUNK = 2.0 * (3 * 64 * 128 * 128 + 3 * 64 * 64 * 128)
@@ -768,8 +776,9 @@ def bench_deltanet_prefill(args, dev, stream, max_over_ranks, barrier, world) ->
             "unit": "tokens/s", "ms_per_step": ms, "n_tokens": T,
             "config": "BASELINE config 4a: 1 x 8192 tokens per GPU, 16 K / 32 V heads, d 128, "
                       "chunk 64, bf16-valued inputs, zero initial state; fp16 hi/lo tensor "
-                      "operands, fp32 accumulation and state; 3 launches per step (per-chunk "
-                      "records, state recurrence, gated norm)",
+                      "operands, fp32 accumulation and state; one call per step = 8 pieces of "
+                      "1024 tokens x 3 launches (per-chunk records, state recurrence, gated "
+                      "norm) on three streams",
             "flops_per_step": flops, "tflops": tflops, "bytes_per_step": nbytes,
             "gbs": nbytes / (ms * 1e-3) / 1e9,
             "roofline": {"bound": "tensor", "achieved": tflops, "peak": pk["bf16_tflops"],
@@ -777,9 +786,12 @@ def bench_deltanet_prefill(args, dev, stream, max_over_ranks, barrier, world) ->
                          "traffic": DN_PREFILL_8K_TRAFFIC,
                          "kernel": "front_kernel + chain_kernel + gate_kernel", "kernel_ms": ms,
                          "peak_source": pk["source"],
+                         "traffic_source": "ncu DRAM bytes of one piece's three launches x 8 "
+                                           "pieces (profiles/deltanet_prefill_tc_8k_ncu.md)",
                          "note": "latency-bound: the state recurrence is sequential over the "
-                                 "128 chunks of each of the 32 heads"},
-            "gpu_launches": 3 * args.steps}
+                                 "128 chunks of each of the 32 heads; the records of each chunk "
+                                 "go through HBM between the front and the chain"},
+            "gpu_launches": 3 * DN_PIECES * args.steps}
 
 
 CP_T = 131072
