@@ -294,6 +294,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float kNegInf = -__int_as_float(0x7f800000);
     float m_ref = kNegInf, l = 0.0f;
     bool ok = true;
+    {
+      // The epilogue's gate rows (this warp's 32 rows, 512 bytes each) into L2 now, so that the
+      // epilogue finds them there: lane = row, four 128-byte lines each.
+      const unsigned rr = 32 * q + lane, tk = t0 + rr / kGroup;
+      if (tk < a.n) {
+        const float* g = a.qg + size_t(tk) * a.qg_stride + (kvh * kGroup + rr % kGroup) * 2 * kDim +
+                         kDim + 128 * hc;
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(g + 32 * e));
+      }
+    }
     // Exchange of one float per row with the partner warp through red[] and an mbarrier with
     // one arrival per warp (bounded wait); returns the partner's value.
     auto exchange = [&](unsigned j, float mine, float& theirs) -> bool {
