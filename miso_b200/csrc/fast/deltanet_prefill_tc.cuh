@@ -453,28 +453,6 @@ __global__ void __launch_bounds__(kFrontThreads, 1)
     for (int i = 0; i < kTok; ++i)
       put4(vt, kTok * warp + i, ch, kBox, yv[i], vt + 2 * kBox);
   }
-  // This CTA's input rows have been read: bring the rows of the unit that will run `ahead` CTAs
-  // later (the next wave, roughly) into L2 while this one computes.
-  // Units run in launch order (chunk fastest, then K head), launch after launch: the unit
-  // `ahead` places later may belong to the next launch (chunks [c0 + gridDim.x, + per)).
-  if (tid == 0) {
-    unsigned nid = blockIdx.y * gridDim.x + blockIdx.x + a.ahead, c2 = nc, kh2 = 0;
-    if (nid < gridDim.x * gridDim.y) {
-      c2 = a.c0 + nid % gridDim.x, kh2 = nid / gridDim.x;
-    } else if (a.c0 + gridDim.x < nc) {
-      const unsigned c1 = a.c0 + gridDim.x, cnt = nc - c1 < a.per ? nc - c1 : a.per;
-      nid -= gridDim.x * gridDim.y;
-      if (nid < cnt * kKHeads)
-        c2 = c1 + nid % cnt, kh2 = nid / cnt;
-    }
-    if (c2 < nc) {
-      const int y0 = int(c2 * kC) - 3;
-      tma_prefetch_2d(&qkvmap, int(kh2 * kDim), y0);
-      tma_prefetch_2d(&qkvmap, int(kQkCh + kh2 * kDim), y0);
-      tma_prefetch_2d(&qkvmap, int(kVCh0 + kh2 * kDim), y0);
-      tma_prefetch_2d(&qkvmap, int(kVCh0 + (kh2 + kKHeads) * kDim), y0);
-    }
-  }
   // The final conv history (the last three input rows) of this unit's channels.
   if (c == nc - 1) {
     for (unsigned u = tid; u < 4 * kDim * 3; u += kFrontThreads) {
@@ -623,6 +601,31 @@ __global__ void __launch_bounds__(kFrontThreads, 1)
       copy_out(sh, a.rec.bh + rec_row(h, c, nc, 192) * kC, kDim, 8, tid, kFrontThreads);
       copy_out(sl, a.rec.bl + rec_row(h, c, nc, 192) * kC, kDim, 8, tid, kFrontThreads);
       __syncthreads();
+    }
+
+    // Bring the input rows of the unit that will run `ahead` CTAs later (the next wave, roughly)
+    // into L2 while this one finishes: issued about two thirds into the CTA, so that the rows are
+    // still in L2 when that unit starts (earlier, the records and the concurrent chain's traffic
+    // evicted them).
+    // Units run in launch order (chunk fastest, then K head), launch after launch: the unit
+    // `ahead` places later may belong to the next launch (chunks [c0 + gridDim.x, + per)).
+    if (tid == 0) {
+      unsigned nid = blockIdx.y * gridDim.x + blockIdx.x + a.ahead, c2 = nc, kh2 = 0;
+      if (nid < gridDim.x * gridDim.y) {
+        c2 = a.c0 + nid % gridDim.x, kh2 = nid / gridDim.x;
+      } else if (a.c0 + gridDim.x < nc) {
+        const unsigned c1 = a.c0 + gridDim.x, cnt = nc - c1 < a.per ? nc - c1 : a.per;
+        nid -= gridDim.x * gridDim.y;
+        if (nid < cnt * kKHeads)
+          c2 = c1 + nid % cnt, kh2 = nid / cnt;
+      }
+      if (c2 < nc) {
+        const int y0 = int(c2 * kC) - 3;
+        tma_prefetch_2d(&qkvmap, int(kh2 * kDim), y0);
+        tma_prefetch_2d(&qkvmap, int(kQkCh + kh2 * kDim), y0);
+        tma_prefetch_2d(&qkvmap, int(kVCh0 + kh2 * kDim), y0);
+        tma_prefetch_2d(&qkvmap, int(kVCh0 + (kh2 + kKHeads) * kDim), y0);
+      }
     }
 
     // ---- F6: T = (I + L)^-1 of both heads, blocked by 16 ------------------------------------
