@@ -61,28 +61,30 @@ class AttentionCp:
                           (rank - k + 1) mod W (this rank's own at k = 1, then those received at
                           step k - 1) and receive from rank - 1 those of rank (rank - k) mod W
                           into the local cache
-    attend(start, n)      causal prefill of query tokens [start, start + n) against the keys
-                          [0, start + n)
+    attend(start, n, after)
+                          causal prefill of query tokens [start, start + n) against the keys
+                          [0, start + n), once ring step `after` has completed (0: no step)
+
+    Every ring step is issued before any attention launch, so the transfers never queue behind
+    attention work; each launch then waits only for the step that completes its keys.
     """
     t: int
     world: int
     rank: int
     prep: Callable[[int, int], None]
     ring_step: Callable[[int], None]
-    attend: Callable[[int, int], None]
+    attend: Callable[[int, int, int], None]
 
     def run(self) -> None:
         low, high = zigzag_chunks(self.t, self.world, self.rank)
         self.prep(*low)
         self.prep(*high)
-        # After step k this rank holds the chunks of ranks rank, rank - 1, ..., rank - k.
-        if self.rank == 0:
-            self.attend(*low)
+        # After step k this rank holds the chunks of ranks rank, rank - 1, ..., rank - k: the low
+        # chunk (keys of ranks 0..rank) needs step `rank`, the high chunk every step.
         for k in range(1, self.world):
             self.ring_step(k)
-            if k == self.rank:
-                self.attend(*low)
-        self.attend(*high)
+        self.attend(*low, self.rank)
+        self.attend(*high, self.world - 1)
 
 
 def ring_sources(world: int, rank: int, k: int) -> tuple[int, int]:
@@ -206,8 +208,8 @@ class GpuAttentionCp:
     """Buffers and kernels of one rank's context-parallel attention prefill over a projection
     buffer proj [t][9216] (the rank reads only its own rows). After run(), self.k / self.v hold
     the whole [2][t][256] fp16 cache on every rank and self.core [t][16][256] the rank's rows.
-    The ring runs on its own stream; `stream` (the compute stream) waits for a step only where
-    an attention launch needs that step's keys."""
+    The ring runs on its own stream, all of its steps issued first; `stream` (the compute
+    stream) waits for a step only where an attention launch needs that step's keys."""
 
     def __init__(self, t: int, world: int, rank: int, proj, q_norm, k_norm, inv_freq,
                  eps: float, stream, group=None):
@@ -224,6 +226,7 @@ class GpuAttentionCp:
         self.core = torch.empty((t, 16, 256), dtype=torch.float32, device=dev)
         self.ring_stream = torch.cuda.Stream(device=dev, priority=-100) if world > 1 else None
         self.prepped = torch.cuda.Event()
+        self.step_done = [torch.cuda.Event() for _ in range(world)]  # [k]: ring step k finished
         self.cp = AttentionCp(t, world, rank, self._prep, self._ring_step, self._attend)
 
     def _prep(self, start: int, n: int) -> None:
@@ -257,13 +260,13 @@ class GpuAttentionCp:
                         ops.append(dist.P2POp(dist.irecv, cache[h, rs:rs + s], prv, self.group))
             for w in dist.batch_isend_irecv(ops):
                 w.wait()  # orders the ring stream after the transfers
-        done = torch.cuda.Event()
-        done.record(self.ring_stream)
-        self.stream.wait_event(done)  # only attention launched after this step waits for it
+        self.step_done[k].record(self.ring_stream)
 
-    def _attend(self, start: int, n: int) -> None:
+    def _attend(self, start: int, n: int, after: int) -> None:
         import ctypes
         capi = self.capi
+        if after > 0:  # the launch follows ring step `after` (its keys are then all present)
+            self.stream.wait_event(self.step_done[after])
         base = self.proj.data_ptr() + start * ATTN_PROJ * 4
         tp = capi.AttnPrefillTcParams(self.q16.data_ptr() + start * 16 * 256 * 2, base,
                                       self.k.data_ptr(), self.v.data_ptr(),

@@ -48,7 +48,7 @@ def attention_case(rank: int, world: int) -> None:
                     req.wait()
                     cache[h, rs:rs + s] = buf
 
-    def attend(start, n):
+    def attend(start, n, after):
         kb = k_loc.numpy().view(np.uint16)
         vb = v_loc.numpy().view(np.uint16)
         out[start:start + n] = oracle.attn_prefill(n, start, q[start:start + n],

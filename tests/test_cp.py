@@ -80,9 +80,9 @@ def test_deltanet_affine_schedule_gloo(world):
 
 @pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
 def test_attention_ring_schedule(world):
-    """Per rank: prep of both own chunks, then W - 1 ring steps; the low chunk r is attended
-    right after step r (rank 0 before the ring), when the keys of ranks 0..r are present, and
-    the high chunk after the last step. The chunks each step forwards are those received at the
+    """Per rank: prep of both own chunks, then all W - 1 ring steps, then the low chunk r
+    attended after step r (rank 0: no step), when the keys of ranks 0..r are present, and the
+    high chunk after the last step. The chunks each step forwards are those received at the
     step before, so after step k a rank holds the chunks of ranks rank, rank - 1, ..., rank - k."""
     t = 64 * world
     for rank in range(world):
@@ -91,13 +91,8 @@ def test_attention_ring_schedule(world):
         cp.AttentionCp(t, world, rank, rec("prep"), rec("ring"), rec("attend")).run()
         low, high = cp.zigzag_chunks(t, world, rank)
         expect = [("prep",) + low, ("prep",) + high]
-        if rank == 0:
-            expect.append(("attend",) + low)
-        for k in range(1, world):
-            expect.append(("ring", k))
-            if k == rank:
-                expect.append(("attend",) + low)
-        expect.append(("attend",) + high)
+        expect += [("ring", k) for k in range(1, world)]
+        expect += [("attend",) + low + (rank,), ("attend",) + high + (world - 1,)]
         assert calls == expect
         held = {rank}
         for k in range(1, world):
