@@ -941,7 +941,14 @@ def bench_cp_block(args, dev, stream, max_over_ranks, barrier, world, rank) -> d
         # rank's DeltaNet could start only once the whole attention layer had been dispatched.
         opts = dist.ProcessGroupNCCL.Options(is_high_priority_stream=True)
         dn_group = dist.new_group(list(range(world)), backend="nccl", pg_options=opts)
-    attn = cp.GpuAttentionCp(t, world, rank, proj, ones, ones, inv, EPS, stream)
+        # The attention's KV ring likewise: each ring step needs every rank's send / receive
+        # kernels, so one rank whose GPU is full of pending attention CTAs would stall the step
+        # for all ranks.
+        ring_group = dist.new_group(list(range(world)), backend="nccl", pg_options=opts)
+    else:
+        ring_group = None
+    attn = cp.GpuAttentionCp(t, world, rank, proj, ones, ones, inv, EPS, stream,
+                             group=ring_group)
     dn = cp.GpuDeltaNetWavefront(t, world, rank, projs, conv_w, ssm_a, dt, norm_w, EPS,
                                  dn_stream, group=dn_group)
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
@@ -950,8 +957,11 @@ def bench_cp_block(args, dev, stream, max_over_ranks, barrier, world, rank) -> d
         if record:
             ev[0].record(stream)
         dn_stream.wait_stream(stream)
-        dn.run()
+        # The attention's prep and KV exchange are enqueued before the DeltaNet fronts (whose
+        # high-priority grids would otherwise be dispatched first and hold the exchange back);
+        # its big attention grids, enqueued here too, yield to the DeltaNet kernels by priority.
         attn.run()
+        dn.run()
         if record:
             ev[1].record(stream)
             ev[2].record(dn_stream)

@@ -3,12 +3,15 @@
 Attention (the gated GQA layer): zig-zag partition of the T tokens into 2W chunks of T / 2W; rank
 r owns chunks r and 2W - 1 - r, which balances the causal work (chunk i costs ~ i + 1/2). Each
 rank runs the prep (norms, RoPE, fp16 KV append) of its own tokens into a full-length KV cache,
-then the ranks pass their chunk pairs around a ring (W - 1 steps of NCCL send / receive over
-NVLink, the only collective of the attention layer; every rank ends up holding the whole cache,
-which the decode phase then reuses). The low chunk r needs only the keys of chunks 0..r, i.e. of
-ranks 0..r, which have arrived after ring step r: its causal tensor-core prefill
-(miso_attn_prefill_tc with pos0 = chunk start) starts then, while the remaining steps are still
-in flight; the high chunk 2W - 1 - r needs every rank's keys and follows the last step.
+then the ranks exchange their chunks directly in two parts (NCCL send / receive over NVLink, the
+only collective of the attention layer; every rank ends up holding the whole cache, which the
+decode phase then reuses): first every rank's low chunk to every other rank, then the high
+chunks. The low chunk r needs only the keys of chunks 0..r, i.e. the low chunks of ranks 0..r:
+its causal tensor-core prefill (miso_attn_prefill_tc with pos0 = chunk start) starts after the
+first part (rank 0's at once), while the second part is in flight; the high chunk 2W - 1 - r
+needs every rank's keys and follows the second part. (A ring of W - 1 dependent steps moves the
+same bytes, but each step is a new NCCL launch that has to find a free SM on every rank while
+long attention CTAs hold them: at W = 8 its steps took ~1 ms each.)
 
 Gated DeltaNet layers: the recurrence needs the state at the end of the previous tokens, so the
 sequence is cut into W contiguous segments and the state is handed from rank r - 1 to rank r.
@@ -19,7 +22,7 @@ recurrences alone. Independent layers form a wavefront: rank r runs layer l's re
 rank r + 1 runs layer l - 1's, so L layers take (W + L - 1) recurrence times.
 
 The orchestration is written against small callables (compute a segment, send / receive a state,
-one ring step of KV chunks) so that the same code runs over NCCL with the CUDA kernels and over
+one part of the KV exchange) so that the same code runs over NCCL with the CUDA kernels and over
 gloo with the CPU oracle in the tests.
 """
 from __future__ import annotations
@@ -57,39 +60,42 @@ class AttentionCp:
     """One rank's share of the context-parallel attention prefill.
 
     prep(start, n)        prep of tokens [start, start + n) into the local full-length cache
-    ring_step(k)          ring step k = 1 .. W - 1: send to rank + 1 the two chunks of rank
-                          (rank - k + 1) mod W (this rank's own at k = 1, then those received at
-                          step k - 1) and receive from rank - 1 those of rank (rank - k) mod W
-                          into the local cache
+    exchange(part)        part 0: send this rank's low chunk to every other rank and receive
+                          theirs into the local cache; part 1: the same for the high chunks
     attend(start, n, after)
                           causal prefill of query tokens [start, start + n) against the keys
-                          [0, start + n), once ring step `after` has completed (0: no step)
+                          [0, start + n), once exchange part `after` has completed (-1: none)
 
-    Every ring step is issued before any attention launch, so the transfers never queue behind
-    attention work; each launch then waits only for the step that completes its keys.
+    Both parts are issued before any attention launch, so the transfers never queue behind
+    attention work; each launch then waits only for the part that completes its keys.
     """
     t: int
     world: int
     rank: int
     prep: Callable[[int, int], None]
-    ring_step: Callable[[int], None]
+    exchange: Callable[[int], None]
     attend: Callable[[int, int, int], None]
 
     def run(self) -> None:
         low, high = zigzag_chunks(self.t, self.world, self.rank)
         self.prep(*low)
         self.prep(*high)
-        # After step k this rank holds the chunks of ranks rank, rank - 1, ..., rank - k: the low
-        # chunk (keys of ranks 0..rank) needs step `rank`, the high chunk every step.
-        for k in range(1, self.world):
-            self.ring_step(k)
-        self.attend(*low, self.rank)
-        self.attend(*high, self.world - 1)
+        if self.world > 1:
+            self.exchange(0)
+            self.exchange(1)
+        # The low chunk needs the low chunks of ranks 0..rank (part 0; rank 0 only its own), the
+        # high chunk every chunk (part 1).
+        self.attend(*low, 0 if self.rank > 0 else -1)
+        self.attend(*high, 1 if self.world > 1 else -1)
 
 
-def ring_sources(world: int, rank: int, k: int) -> tuple[int, int]:
-    """(rank whose chunks this rank forwards, rank whose chunks it receives) at ring step k."""
-    return (rank - k + 1) % world, (rank - k) % world
+def exchange_chunks(t: int, world: int, rank: int, part: int) -> list[tuple[int, int, int]]:
+    """(peer, start of this rank's chunk it sends, start of the peer's chunk it receives) for
+    every other rank, in exchange part `part` (0: the low chunks, 1: the high ones)."""
+    s = t // (2 * world)
+    mine = zigzag_chunks(t, world, rank)[part][0]
+    return [(peer, mine, zigzag_chunks(t, world, peer)[part][0]) for peer in range(world)
+            if peer != rank] if s > 0 else []
 
 
 @dataclass
@@ -208,8 +214,8 @@ class GpuAttentionCp:
     """Buffers and kernels of one rank's context-parallel attention prefill over a projection
     buffer proj [t][9216] (the rank reads only its own rows). After run(), self.k / self.v hold
     the whole [2][t][256] fp16 cache on every rank and self.core [t][16][256] the rank's rows.
-    The ring runs on its own stream, all of its steps issued first; `stream` (the compute
-    stream) waits for a step only where an attention launch needs that step's keys."""
+    The exchange runs on its own stream, both of its parts issued first; `stream` (the compute
+    stream) waits for a part only where an attention launch needs that part's keys."""
 
     def __init__(self, t: int, world: int, rank: int, proj, q_norm, k_norm, inv_freq,
                  eps: float, stream, group=None):
@@ -224,10 +230,10 @@ class GpuAttentionCp:
         self.v = torch.zeros_like(self.k)
         self.q16 = torch.empty((t, 16, 256), dtype=torch.float16, device=dev)
         self.core = torch.empty((t, 16, 256), dtype=torch.float32, device=dev)
-        self.ring_stream = torch.cuda.Stream(device=dev, priority=-100) if world > 1 else None
+        self.xchg_stream = torch.cuda.Stream(device=dev, priority=-100) if world > 1 else None
         self.prepped = torch.cuda.Event()
-        self.step_done = [torch.cuda.Event() for _ in range(world)]  # [k]: ring step k finished
-        self.cp = AttentionCp(t, world, rank, self._prep, self._ring_step, self._attend)
+        self.part_done = [torch.cuda.Event() for _ in range(2)]  # exchange part finished
+        self.cp = AttentionCp(t, world, rank, self._prep, self._exchange, self._attend)
 
     def _prep(self, start: int, n: int) -> None:
         import ctypes
@@ -242,31 +248,30 @@ class GpuAttentionCp:
             ctypes.byref(bp), self.q16.data_ptr() + start * 16 * 256 * 2, self.stream.cuda_stream))
         self.prepped.record(self.stream)  # after the second prep: both own chunks are in place
 
-    def _ring_step(self, k: int) -> None:
+    def _exchange(self, part: int) -> None:
         import torch
         import torch.distributed as dist
-        if k == 1:  # the own chunks are sent once prepped (not after any attention queued since)
-            self.ring_stream.wait_event(self.prepped)
-        fwd, src = ring_sources(self.world, self.rank, k)
+        if part == 0:  # the own chunks are sent once prepped (not after any attention queued since)
+            self.xchg_stream.wait_event(self.prepped)
         s = self.t // (2 * self.world)
-        nxt, prv = (self.rank + 1) % self.world, (self.rank - 1) % self.world
         ops = []
-        with torch.cuda.stream(self.ring_stream):
-            for (fs, _), (rs, _) in zip(zigzag_chunks(self.t, self.world, fwd),
-                                        zigzag_chunks(self.t, self.world, src)):
+        with torch.cuda.stream(self.xchg_stream):
+            for peer, mine, theirs in exchange_chunks(self.t, self.world, self.rank, part):
                 for cache in (self.k, self.v):
                     for h in range(2):
-                        ops.append(dist.P2POp(dist.isend, cache[h, fs:fs + s], nxt, self.group))
-                        ops.append(dist.P2POp(dist.irecv, cache[h, rs:rs + s], prv, self.group))
+                        ops.append(dist.P2POp(dist.isend, cache[h, mine:mine + s], peer,
+                                              self.group))
+                        ops.append(dist.P2POp(dist.irecv, cache[h, theirs:theirs + s], peer,
+                                              self.group))
             for w in dist.batch_isend_irecv(ops):
-                w.wait()  # orders the ring stream after the transfers
-        self.step_done[k].record(self.ring_stream)
+                w.wait()  # orders the exchange stream after the transfers
+        self.part_done[part].record(self.xchg_stream)
 
     def _attend(self, start: int, n: int, after: int) -> None:
         import ctypes
         capi = self.capi
-        if after > 0:  # the launch follows ring step `after` (its keys are then all present)
-            self.stream.wait_event(self.step_done[after])
+        if after >= 0:  # the launch follows exchange part `after` (its keys are then present)
+            self.stream.wait_event(self.part_done[after])
         base = self.proj.data_ptr() + start * ATTN_PROJ * 4
         tp = capi.AttnPrefillTcParams(self.q16.data_ptr() + start * 16 * 256 * 2, base,
                                       self.k.data_ptr(), self.v.data_ptr(),

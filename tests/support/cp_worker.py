@@ -34,19 +34,20 @@ def attention_case(rank: int, world: int) -> None:
         k_loc[:, start:start + n] = torch.from_numpy(k_full[:, start:start + n])
         v_loc[:, start:start + n] = torch.from_numpy(v_full[:, start:start + n])
 
-    def ring_step(k):
-        fwd, src = cp.ring_sources(world, rank, k)
+    def exchange(part):
         s = t // (2 * world)
-        nxt, prv = (rank + 1) % world, (rank - 1) % world
-        for (fs, _), (rs, _) in zip(cp.zigzag_chunks(t, world, fwd),
-                                    cp.zigzag_chunks(t, world, src)):
+        # Pairwise in a fixed order (lower rank sends first) so that blocking gloo calls pair up.
+        for peer, mine, theirs in cp.exchange_chunks(t, world, rank, part):
             for cache in (k_loc, v_loc):
                 for h in range(2):
-                    req = dist.isend(cache[h, fs:fs + s].contiguous(), nxt)
                     buf = torch.empty((s, 256), dtype=torch.float16)
-                    dist.recv(buf, prv)
-                    req.wait()
-                    cache[h, rs:rs + s] = buf
+                    if rank < peer:
+                        dist.send(cache[h, mine:mine + s].contiguous(), peer)
+                        dist.recv(buf, peer)
+                    else:
+                        dist.recv(buf, peer)
+                        dist.send(cache[h, mine:mine + s].contiguous(), peer)
+                    cache[h, theirs:theirs + s] = buf
 
     def attend(start, n, after):
         kb = k_loc.numpy().view(np.uint16)
@@ -54,7 +55,7 @@ def attention_case(rank: int, world: int) -> None:
         out[start:start + n] = oracle.attn_prefill(n, start, q[start:start + n],
                                                    qg[start:start + n], 8192, kb, vb, t)
 
-    cp.AttentionCp(t, world, rank, prep, ring_step, attend).run()
+    cp.AttentionCp(t, world, rank, prep, exchange, attend).run()
     # Every rank now holds the whole cache.
     assert np.array_equal(k_loc.numpy(), k_full) and np.array_equal(v_loc.numpy(), v_full)
     total = torch.from_numpy(out)

@@ -1,6 +1,6 @@
 """Context-parallel prefill (miso_b200.cp): the partition arithmetic, and the multi-rank
 orchestration run as gloo ranks on the CPU with the oracle in place of the kernels (attention:
-zig-zag chunks + ring KV exchange; DeltaNet: state hand-off wavefront), bit-exact against a
+zig-zag chunks + direct KV exchange; DeltaNet: state hand-off wavefront), bit-exact against a
 single-process run."""
 import os
 import socket
@@ -79,29 +79,37 @@ def test_deltanet_affine_schedule_gloo(world):
 
 
 @pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
-def test_attention_ring_schedule(world):
-    """Per rank: prep of both own chunks, then all W - 1 ring steps, then the low chunk r
-    attended after step r (rank 0: no step), when the keys of ranks 0..r are present, and the
-    high chunk after the last step. The chunks each step forwards are those received at the
-    step before, so after step k a rank holds the chunks of ranks rank, rank - 1, ..., rank - k."""
+def test_attention_exchange_schedule(world):
+    """Per rank: prep of both own chunks, then the two exchange parts (low chunks, high chunks),
+    then the low chunk r attended after part 0 (rank 0: without waiting), when the keys of
+    chunks 0..r are present, and the high chunk after part 1. Part p sends this rank's chunk p to
+    every other rank and receives theirs, so afterwards every rank holds every chunk."""
     t = 64 * world
+    s = t // (2 * world)
     for rank in range(world):
         calls = []
         rec = lambda name: (lambda *a: calls.append((name,) + a))  # noqa: E731
-        cp.AttentionCp(t, world, rank, rec("prep"), rec("ring"), rec("attend")).run()
+        cp.AttentionCp(t, world, rank, rec("prep"), rec("exchange"), rec("attend")).run()
         low, high = cp.zigzag_chunks(t, world, rank)
         expect = [("prep",) + low, ("prep",) + high]
-        expect += [("ring", k) for k in range(1, world)]
-        expect += [("attend",) + low + (rank,), ("attend",) + high + (world - 1,)]
+        if world > 1:
+            expect += [("exchange", 0), ("exchange", 1)]
+        expect += [("attend",) + low + (0 if rank > 0 else -1,),
+                   ("attend",) + high + (1 if world > 1 else -1,)]
         assert calls == expect
-        held = {rank}
-        for k in range(1, world):
-            fwd, src = cp.ring_sources(world, rank, k)
-            assert fwd in held  # forwards what it already holds
-            held.add(src)
-            if k == rank:  # the low chunk's keys: chunks 0..rank, owned by ranks 0..rank
-                assert set(range(rank + 1)) <= held
-        assert held == set(range(world))
+        held = {low[0], high[0]}
+        for part in (0, 1):
+            pairs = cp.exchange_chunks(t, world, rank, part)
+            assert sorted(p for p, _, _ in pairs) == [p for p in range(world) if p != rank]
+            for peer, mine, theirs in pairs:
+                assert mine == (low, high)[part][0]
+                assert theirs == cp.zigzag_chunks(t, world, peer)[part][0]
+                # symmetric: the peer sends this rank exactly what this rank receives
+                assert (rank, theirs, mine) in cp.exchange_chunks(t, world, peer, part)
+                held.add(theirs)
+            if part == 0:  # the low chunk's keys: chunks 0..rank
+                assert {c * s for c in range(rank + 1)} <= held
+        assert held == {c * s for c in range(2 * world)}
 
 
 @pytest.mark.parametrize("world", [1, 2, 4])
