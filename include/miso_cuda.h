@@ -368,6 +368,15 @@ int miso_deltanet_prefill_tc_front(const miso_deltanet_seq_params* p, void* scra
 int miso_deltanet_prefill_tc_recur(const miso_deltanet_seq_params* p, void* scratch,
                                    size_t scratch_bytes, void* stream);
 
+/* The two parts of _recur, for callers whose next step needs only the state: _chain runs the
+ * recurrence (reads the scratch of a _front call, z is not read; writes the state and the
+ * pre-norm outputs to out), _gate then applies the gated RMS norm to out in place (reads z and
+ * norm_w; scratch is only validated). _chain followed by _gate equals _recur bit for bit. */
+int miso_deltanet_prefill_tc_chain(const miso_deltanet_seq_params* p, void* scratch,
+                                   size_t scratch_bytes, void* stream);
+int miso_deltanet_prefill_tc_gate(const miso_deltanet_seq_params* p, void* scratch,
+                                  size_t scratch_bytes, void* stream);
+
 /* ---------------------------------------------------------------------------------------------
  * Library state
  * ------------------------------------------------------------------------------------------- */

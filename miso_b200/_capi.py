@@ -117,6 +117,10 @@ SIGNATURES = {
                                                  _P]),
     "miso_deltanet_prefill_tc_recur": (C.c_int, [C.POINTER(DeltaNetSeqParams), _P, C.c_size_t,
                                                  _P]),
+    "miso_deltanet_prefill_tc_chain": (C.c_int, [C.POINTER(DeltaNetSeqParams), _P, C.c_size_t,
+                                                 _P]),
+    "miso_deltanet_prefill_tc_gate": (C.c_int, [C.POINTER(DeltaNetSeqParams), _P, C.c_size_t,
+                                                _P]),
     "miso_attn_prep_batch_f16": (C.c_int, [C.POINTER(AttnPrepBatchParams), _P, _P]),
     "miso_device_status": (C.c_int, [C.c_int, C.POINTER(C.c_int)]),
     "miso_version": (C.c_char_p, []),

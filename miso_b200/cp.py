@@ -290,10 +290,11 @@ class GpuDeltaNetWavefront:
     """Buffers and kernels of one rank's share of L independent DeltaNet layers over projection
     buffers projs[l] [t][12352]: the rank runs miso_deltanet_prefill_tc_front on its contiguous
     segment of every layer as soon as the conv halo (the three input rows before the segment)
-    has arrived, then, per layer, miso_deltanet_prefill_tc_recur from the state received from
-    rank - 1, and passes the state on to rank + 1. After run(), self.state[l] / self.conv[l] hold
-    the layer's state and conv history after the rank's segment (those of the whole sequence on
-    the last rank) and self.out[l] [t][4096] its rows."""
+    has arrived, then, per layer, miso_deltanet_prefill_tc_chain from the state received from
+    rank - 1, passes the state on to rank + 1 and applies the gated norm
+    (miso_deltanet_prefill_tc_gate) on a stream of its own, off the hand-off's path. After run(),
+    self.state[l] / self.conv[l] hold the layer's state and conv history after the rank's
+    segment (those of the whole sequence on the last rank) and self.out[l] [t][4096] its rows."""
 
     def __init__(self, t: int, world: int, rank: int, projs, conv_w, ssm_a, dt_bias, norm_w,
                  eps: float, stream, group=None):
@@ -318,6 +319,8 @@ class GpuDeltaNetWavefront:
         self.front_stream = torch.cuda.Stream(device=dev, priority=-100)
         self.halo_done = torch.cuda.Event()
         self.front_done = [torch.cuda.Event() for _ in range(L)]
+        self.chain_done = [torch.cuda.Event() for _ in range(L)]
+        self.gate_stream = torch.cuda.Stream(device=dev)
         self.wf = DeltaNetWavefront(t, world, rank, L, self._front, self._recur, self._reset,
                                     self._halo_recv, self._halo_send, self._recv, self._send)
 
@@ -350,8 +353,15 @@ class GpuDeltaNetWavefront:
         import ctypes
         self.stream.wait_event(self.front_done[layer])
         p = self._params(layer, start, n)
-        self.capi.check("miso_deltanet_prefill_tc_recur", self.lib.miso_deltanet_prefill_tc_recur(
+        self.capi.check("miso_deltanet_prefill_tc_chain", self.lib.miso_deltanet_prefill_tc_chain(
             ctypes.byref(p), self.scratch[layer].data_ptr(), self.sb, self.stream.cuda_stream))
+        # The state is final after the chain: the hand-off (on self.stream) does not wait for the
+        # gated norm of the outputs, which runs on its own stream.
+        self.chain_done[layer].record(self.stream)
+        self.gate_stream.wait_event(self.chain_done[layer])
+        self.capi.check("miso_deltanet_prefill_tc_gate", self.lib.miso_deltanet_prefill_tc_gate(
+            ctypes.byref(p), self.scratch[layer].data_ptr(), self.sb,
+            self.gate_stream.cuda_stream))
 
     def _reset(self, layer: int) -> None:
         self.state[layer].zero_()
@@ -381,3 +391,4 @@ class GpuDeltaNetWavefront:
         import torch
         with torch.cuda.stream(self.stream):
             self.wf.run()
+        self.stream.wait_stream(self.gate_stream)  # the outputs are complete after run()

@@ -651,7 +651,8 @@ namespace {
 
 // Stages of the tensor-core DeltaNet prefill: bit 0 = front_kernel (conv, norms and every
 // state-independent product of each chunk; no state access), bit 1 = chain_kernel (the state
-// recurrence and the outputs, from the records bit 0 wrote).
+// recurrence and the pre-norm outputs, from the records bit 0 wrote), bit 2 = gate_kernel (the
+// gated RMS norm of the outputs).
 int dn_prefill_tc(const miso_deltanet_seq_params* p, void* scratch, size_t scratch_bytes,
                   void* stream, int stages) {
   namespace pf = miso::fast::dnpf;
@@ -746,12 +747,12 @@ int dn_prefill_tc(const miso_deltanet_seq_params* p, void* scratch, size_t scrat
     ca.out = p->out;
     ca.n = p->n;
     ca.nc = nc;
-    ga.out = p->out;
-    ga.z = p->z;
-    ga.norm_w = p->norm_w;
-    ga.zab_stride = p->zab_stride;
-    ga.eps = p->eps;
   }
+  ga.out = p->out;
+  ga.z = p->z;
+  ga.norm_w = p->norm_w;
+  ga.zab_stride = p->zab_stride;
+  ga.eps = p->eps;
   // Chunks [c0, c0 + cnt) of each stage.
   auto front = [&](cudaStream_t q, unsigned c0, unsigned cnt) {
     pf::FrontArgs f = fa;
@@ -778,10 +779,12 @@ int dn_prefill_tc(const miso_deltanet_seq_params* p, void* scratch, size_t scrat
     return launch_status();
   };
 
-  if (stages != 3 || nc <= kDnPieceChunks) {
+  if (stages != 7 || nc <= kDnPieceChunks) {
     if ((stages & 1) && (st = front(s, 0, nc)) != MISO_OK)
       return st;
-    if ((stages & 2) && ((st = chain(s, 0, nc)) != MISO_OK || (st = gate(s, 0, nc)) != MISO_OK))
+    if ((stages & 2) && (st = chain(s, 0, nc)) != MISO_OK)
+      return st;
+    if ((stages & 4) && (st = gate(s, 0, nc)) != MISO_OK)
       return st;
     return MISO_OK;
   }
@@ -832,7 +835,7 @@ extern "C" {
 
 int miso_deltanet_prefill_tc(const miso_deltanet_seq_params* p, void* scratch, size_t scratch_bytes,
                              void* stream) {
-  return dn_prefill_tc(p, scratch, scratch_bytes, stream, 3);
+  return dn_prefill_tc(p, scratch, scratch_bytes, stream, 7);
 }
 
 int miso_deltanet_prefill_tc_front(const miso_deltanet_seq_params* p, void* scratch,
@@ -842,7 +845,17 @@ int miso_deltanet_prefill_tc_front(const miso_deltanet_seq_params* p, void* scra
 
 int miso_deltanet_prefill_tc_recur(const miso_deltanet_seq_params* p, void* scratch,
                                    size_t scratch_bytes, void* stream) {
+  return dn_prefill_tc(p, scratch, scratch_bytes, stream, 2 | 4);
+}
+
+int miso_deltanet_prefill_tc_chain(const miso_deltanet_seq_params* p, void* scratch,
+                                   size_t scratch_bytes, void* stream) {
   return dn_prefill_tc(p, scratch, scratch_bytes, stream, 2);
+}
+
+int miso_deltanet_prefill_tc_gate(const miso_deltanet_seq_params* p, void* scratch,
+                                  size_t scratch_bytes, void* stream) {
+  return dn_prefill_tc(p, scratch, scratch_bytes, stream, 4);
 }
 
 }  // extern "C"

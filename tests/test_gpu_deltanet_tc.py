@@ -21,8 +21,9 @@ DEV = torch.device("cuda")
 
 
 def run_tc(x, state=None, conv_in=None, split=False):
-    """One miso_deltanet_prefill_tc call, or (split=True) the _front / _recur pair with a scratch
-    buffer whose previous contents are garbage and a state that the front must not touch."""
+    """One miso_deltanet_prefill_tc call, or (split=True) the _front / _recur pair, or
+    (split="chain") _front, _chain and _gate, with a scratch buffer whose previous contents are
+    garbage and a state that the front must not touch."""
     n = x["n"]
     lib = capi.load()
     d = {k: T(x[k]) for k in ("qkv", "zab", "conv_w", "ssm_a", "dt", "norm_w")}
@@ -44,8 +45,14 @@ def run_tc(x, state=None, conv_in=None, split=False):
                    lib.miso_deltanet_prefill_tc_front(C.byref(p), ptr(scratch), sb, None))
         torch.cuda.synchronize()
         assert torch.equal(st, st_before), "the front stage wrote the state"
-        capi.check("miso_deltanet_prefill_tc_recur",
-                   lib.miso_deltanet_prefill_tc_recur(C.byref(p), ptr(scratch), sb, None))
+        if split == "chain":
+            capi.check("miso_deltanet_prefill_tc_chain",
+                       lib.miso_deltanet_prefill_tc_chain(C.byref(p), ptr(scratch), sb, None))
+            capi.check("miso_deltanet_prefill_tc_gate",
+                       lib.miso_deltanet_prefill_tc_gate(C.byref(p), ptr(scratch), sb, None))
+        else:
+            capi.check("miso_deltanet_prefill_tc_recur",
+                       lib.miso_deltanet_prefill_tc_recur(C.byref(p), ptr(scratch), sb, None))
     else:
         capi.check("miso_deltanet_prefill_tc",
                    lib.miso_deltanet_prefill_tc(C.byref(p), ptr(scratch), sb, None))
@@ -136,13 +143,16 @@ def test_prefill_tc_chained_calls_hand_off_state_and_history():
 @pytest.mark.parametrize("n", [5, 64, 300, 2048])
 def test_front_then_recur_equals_one_call_bitwise(n):
     """The two-stage form used by the context-parallel wavefront (conv + tiles first, the
-    recurrence once the state is there) gives the one-call results bit for bit."""
+    recurrence once the state is there), and that recurrence split into the chain and the gated
+    norm, give the one-call results bit for bit."""
     x = config4a_inputs(n, seed=3)
     x["state"] = (0.1 * np.random.RandomState(4).standard_normal((32, 128, 128))).astype(np.float32)
     x["conv_in"] = np.random.RandomState(5).standard_normal((8192, 3)).astype(np.float32)
     o1, s1, c1 = run_tc(x)
     o2, s2, c2 = run_tc(x, split=True)
     assert np.array_equal(o1, o2) and np.array_equal(s1, s2) and np.array_equal(c1, c2)
+    o3, s3, c3 = run_tc(x, split="chain")
+    assert np.array_equal(o1, o3) and np.array_equal(s1, s3) and np.array_equal(c1, c3)
     assert status_clear()
 
 
