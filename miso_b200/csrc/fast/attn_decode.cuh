@@ -325,13 +325,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __threadfence();
       dev::named_bar_sync(1, kConsumers);
-      if (tid == 0) {
-        // CTAs between the segment's first and last owner may have empty ranges (T < P).
+      if (warp == 0) {
+        // CTAs between the segment's first and last owner may have empty ranges (T < P): warp 0
+        // counts the non-empty ones (the range bounds take 64-bit divisions), lane 0 arrives.
         int parts = 0;
-        for (unsigned cc = c_first; cc <= c_last; ++cc)
+        for (unsigned cc = c_first + lane; cc <= c_last; cc += 32)
           parts += range_begin(cc, T, P) < range_begin(cc + 1, T, P);
-        const int prev = atomicAdd(&a.counters[seg], 1);
-        sm.is_last = prev == parts - 1;
+        parts = __reduce_add_sync(0xffffffffu, parts);
+        if (lane == 0) {
+          const int prev = atomicAdd(&a.counters[seg], 1);
+          sm.is_last = prev == parts - 1;
+        }
       }
       dev::named_bar_sync(1, kConsumers);
       if (sm.is_last) {
@@ -358,6 +362,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         // in lane 0, in partial order, L[h] = sum_k w[k][h] l_k.
         float* wts = sm.slot[0];             // [np][kGroup]
         float* Ls = sm.slot[0] + np * kGroup;  // [kGroup]
+        // The partials' l values [np][kGroup], loaded by all lanes at once into the Q fragment
+        // area (idle until the next segment), so that lane 0's ordered sum reads shared memory.
+        float* lks = reinterpret_cast<float*>(sm.qfrag);
         {
           const unsigned h = warp;
           float M = kNegInf;
@@ -371,30 +378,45 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float* pp = part_of(k);
             const float mc = pp ? __ldcg(pp + h) : kNegInf;
             wts[k * kGroup + h] = mc == kNegInf ? 0.0f : fast_exp(mc - M);
+            lks[k * kGroup + h] = pp ? __ldcg(pp + kGroup + h) : 0.0f;
           }
           __syncwarp();
           if (lane == 0) {
             float L = 0.0f;
             for (unsigned k = 0; k < np; ++k)
-              if (const float* pp = part_of(k))
-                L += wts[k * kGroup + h] * __ldcg(pp + kGroup + h);
+              if (poff[k] >= 0)
+                L += wts[k * kGroup + h] * lks[k * kGroup + h];
             Ls[h] = L;
           }
         }
         dev::named_bar_sync(1, kConsumers);
         // Outputs: thread tid takes dimension tid of every head (eight independent sums, each
         // in partial order), so 8 x 4 loads are in flight at once.
+        // Eight partials' values are loaded before any is accumulated (64 loads in flight per
+        // thread); the sums still run over the partials in order.
         float ov[kGroup];
 #pragma unroll
         for (unsigned h = 0; h < kGroup; ++h)
           ov[h] = 0.0f;
-#pragma unroll 4
-        for (unsigned k = 0; k < np; ++k)
-          if (const float* pp = part_of(k)) {
+        constexpr unsigned kBatch = 8;
+#pragma unroll 1
+        for (unsigned k0 = 0; k0 < np; k0 += kBatch) {
+          float x[kBatch][kGroup];
+#pragma unroll
+          for (unsigned j = 0; j < kBatch; ++j) {
+            const float* pp = k0 + j < np ? part_of(k0 + j) : nullptr;
 #pragma unroll
             for (unsigned h = 0; h < kGroup; ++h)
-              ov[h] += wts[k * kGroup + h] * __ldcg(pp + 2 * kGroup + h * kDim + tid);
+              x[j][h] = pp ? __ldcg(pp + 2 * kGroup + h * kDim + tid) : 0.0f;
           }
+#pragma unroll
+          for (unsigned j = 0; j < kBatch; ++j)
+            if (k0 + j < np && poff[k0 + j] >= 0) {
+#pragma unroll
+              for (unsigned h = 0; h < kGroup; ++h)
+                ov[h] += wts[(k0 + j) * kGroup + h] * x[j][h];
+            }
+        }
 #pragma unroll
         for (unsigned h = 0; h < kGroup; ++h)
           out[h * kDim + tid] = ov[h] / Ls[h] / (1.0f + fast_exp(-gate[h * 2 * kDim + tid]));
