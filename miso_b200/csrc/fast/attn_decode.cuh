@@ -45,7 +45,7 @@ constexpr int kBoxBytes = 64 * 128;            // TMA box: 64 rows x 64 dims fp1
 constexpr int kHalfStage = 4 * kBoxBytes;      // K (or V) of one tile
 constexpr int kStageBytes = 2 * kHalfStage;    // 64 KiB
 constexpr int kMaxBatch = 1024;
-constexpr unsigned kMinTiles = 2;              // fewest tiles a working CTA takes
+constexpr unsigned kMinTiles = 4;              // fewest tiles a working CTA takes
 constexpr unsigned kMaxCtas = 256;             // grid limit: the merge weights fit one slot
 constexpr int kSlotRow = 260;                  // padded [head][dim] row of a merge slot (floats)
 constexpr int kSlotFloats = kGroup * kSlotRow + kGroup;  // o[8][260] then l[8]
@@ -392,34 +392,41 @@ __global__ void __launch_bounds__(kThreads, 1)
         dev::named_bar_sync(1, kConsumers);
         // Outputs: thread tid takes dimension tid of every head (eight independent sums, each
         // in partial order), so 8 x 4 loads are in flight at once.
-        // Eight partials' values are loaded before any is accumulated (64 loads in flight per
-        // thread); the sums still run over the partials in order.
-        float ov[kGroup];
+        // Warp h takes head h, lane l dimensions [8 l, 8 l + 8): two 16-byte loads per partial.
+        // Eight partials' values are loaded before any is accumulated; each output's sum still
+        // runs over the partials in order.
+        {
+          const unsigned h = warp, d0 = 8 * lane;
+          float ov[8];
 #pragma unroll
-        for (unsigned h = 0; h < kGroup; ++h)
-          ov[h] = 0.0f;
-        constexpr unsigned kBatch = 8;
+          for (int e = 0; e < 8; ++e)
+            ov[e] = 0.0f;
+          constexpr unsigned kBatch = 8;
 #pragma unroll 1
-        for (unsigned k0 = 0; k0 < np; k0 += kBatch) {
-          float x[kBatch][kGroup];
+          for (unsigned k0 = 0; k0 < np; k0 += kBatch) {
+            float4 x[kBatch][2];
 #pragma unroll
-          for (unsigned j = 0; j < kBatch; ++j) {
-            const float* pp = k0 + j < np ? part_of(k0 + j) : nullptr;
+            for (unsigned j = 0; j < kBatch; ++j) {
+              const float* pp = k0 + j < np ? part_of(k0 + j) : nullptr;
+              const float4* src = reinterpret_cast<const float4*>(pp + 2 * kGroup + h * kDim + d0);
+              x[j][0] = pp ? __ldcg(src) : make_float4(0.f, 0.f, 0.f, 0.f);
+              x[j][1] = pp ? __ldcg(src + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
 #pragma unroll
-            for (unsigned h = 0; h < kGroup; ++h)
-              x[j][h] = pp ? __ldcg(pp + 2 * kGroup + h * kDim + tid) : 0.0f;
+            for (unsigned j = 0; j < kBatch; ++j)
+              if (k0 + j < np && poff[k0 + j] >= 0) {
+                const float w = wts[(k0 + j) * kGroup + h];
+                ov[0] += w * x[j][0].x, ov[1] += w * x[j][0].y;
+                ov[2] += w * x[j][0].z, ov[3] += w * x[j][0].w;
+                ov[4] += w * x[j][1].x, ov[5] += w * x[j][1].y;
+                ov[6] += w * x[j][1].z, ov[7] += w * x[j][1].w;
+              }
           }
 #pragma unroll
-          for (unsigned j = 0; j < kBatch; ++j)
-            if (k0 + j < np && poff[k0 + j] >= 0) {
-#pragma unroll
-              for (unsigned h = 0; h < kGroup; ++h)
-                ov[h] += wts[(k0 + j) * kGroup + h] * x[j][h];
-            }
+          for (int e = 0; e < 8; ++e)
+            out[h * kDim + d0 + e] =
+                ov[e] / Ls[h] / (1.0f + fast_exp(-gate[h * 2 * kDim + d0 + e]));
         }
-#pragma unroll
-        for (unsigned h = 0; h < kGroup; ++h)
-          out[h * kDim + tid] = ov[h] / Ls[h] / (1.0f + fast_exp(-gate[h * 2 * kDim + tid]));
         if (tid == 0)
           a.counters[seg] = 0;  // ready for the next call
       }
