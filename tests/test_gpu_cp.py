@@ -1,5 +1,5 @@
 """Multi-GPU context-parallel prefill over NCCL (one process per GPU): attention zig-zag chunks
-with the ring KV exchange, and the DeltaNet state hand-off wavefront, bit-identical to the
+with the direct KV exchange, and the DeltaNet state hand-off wavefront, bit-identical to the
 single-GPU kernels over the whole sequence. Needs at least two GPUs (skipped otherwise)."""
 import os
 import socket
