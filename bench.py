@@ -563,9 +563,10 @@ DECODE_TRAFFIC_PER_ALGORITHMIC_BYTE = (257.0 + 6.3) / 256.8
 # ncu DRAM bytes (read + write) of one full-size launch (profiles/prefill_kernel_8k_ncu.md,
 # profiles/deltanet_prefill_tc_8k_ncu.md).
 PREFILL_8K_TRAFFIC = (221.3 + 101.5) * 1e6
-# DRAM bytes (read + write inside each launch) of the three kernels of one piece of 1024 tokens
+# DRAM bytes (read + write inside each launch) of the three kernels of a piece of 1024 tokens
 # (front 49.9 + 15.8 MB, chain 69.3 + 3.1 MB, gate 33.6 + 0.0 MB; ncu, caches flushed before each
-# launch), times the 8 pieces of a call at 8192 tokens.
+# launch), times the 8 such token ranges of a call at 8192 tokens (every byte is per token: the
+# records are written and read once whatever the piece size).
 DN_PREFILL_8K_TRAFFIC = 8 * (49.94 + 15.80 + 69.26 + 3.08 + 33.56) * 1e6
 # DRAM bytes inside one launch of step_batched_kernel at batch 64 (ncu: read 143.9 MB, write
 # 87.6 MB; the remaining state writes leave L2 after the launch ends).
@@ -714,7 +715,7 @@ def bench_deltanet_step(args, dev, stream, max_over_ranks, barrier, world) -> di
 
 
 DN_PREFILL_T = 8192
-DN_PIECES = -(-(DN_PREFILL_T // 64) // 16)  # pieces of 16 chunks per miso_deltanet_prefill_tc call
+DN_PIECES = -(-(DN_PREFILL_T // 64) // 32)  # pieces of 32 chunks per miso_deltanet_prefill_tc call
 # Algorithmic FLOPs of the chunked rule per (V head, chunk of 64): 2 (3 C d^2 + 3 C^2 d)
 # = 9.44 MFLOP (QK^T / KK^T, the UT-transform products, S updates), 32 heads x T / 64 chunks.
 DN_PREFILL_FLOPS_PER_HEAD_CHUNK = 2.0 * (3 * 64 * 128 * 128 + 3 * 64 * 64 * 128)
@@ -776,8 +777,8 @@ def bench_deltanet_prefill(args, dev, stream, max_over_ranks, barrier, world) ->
             "unit": "tokens/s", "ms_per_step": ms, "n_tokens": T,
             "config": "BASELINE config 4a: 1 x 8192 tokens per GPU, 16 K / 32 V heads, d 128, "
                       "chunk 64, bf16-valued inputs, zero initial state; fp16 hi/lo tensor "
-                      "operands, fp32 accumulation and state; one call per step = 8 pieces of "
-                      "1024 tokens x 3 launches (per-chunk records, state recurrence, gated "
+                      "operands, fp32 accumulation and state; one call per step = 4 pieces of "
+                      "2048 tokens x 3 launches (per-chunk records, state recurrence, gated "
                       "norm) on three streams",
             "flops_per_step": flops, "tflops": tflops, "bytes_per_step": nbytes,
             "gbs": nbytes / (ms * 1e-3) / 1e9,
