@@ -805,7 +805,7 @@ def cp_block_decode(args, dev, stream, max_over_ranks, barrier, world, rank, att
                     g) -> dict:
     """BASELINE config 5 (decode part): 256 decode steps of the block at a total batch of 8
     sequences that continue from the context-parallel prefix. The 8 sequences are split over the
-    ranks; each rank already holds the whole prefix KV cache (from the prefill's KV ring) and
+    ranks; each rank already holds the whole prefix KV cache (from the prefill's KV exchange) and
     receives the DeltaNet states at the end of the prefix from the last rank (a broadcast). Step
     = batched attention prep + split-K decode, then the batched DeltaNet step of each layer."""
     import torch
@@ -911,7 +911,7 @@ def bench_cp_block(args, dev, stream, max_over_ranks, barrier, world, rank) -> d
     """BASELINE config 5 (prefill part): one hybrid block (3 Gated DeltaNet + 1 gated GQA layer,
     independent seeded bf16-valued N(0,1) mixer inputs, no projections) over one sequence of
     T = 131072 tokens, context-parallel over the ranks: attention with zig-zag chunks and the KV
-    ring KV exchange, DeltaNet with the state hand-off wavefront (miso_b200.cp). At one GPU the same
+    direct KV exchange, DeltaNet with the state hand-off wavefront (miso_b200.cp). At one GPU the same
     code runs the whole sequence locally. Step = the block's prefill; tokens/s = T / step."""
     import torch
     from miso_b200 import attention as A
@@ -942,8 +942,8 @@ def bench_cp_block(args, dev, stream, max_over_ranks, barrier, world, rank) -> d
         # rank's DeltaNet could start only once the whole attention layer had been dispatched.
         opts = dist.ProcessGroupNCCL.Options(is_high_priority_stream=True)
         dn_group = dist.new_group(list(range(world)), backend="nccl", pg_options=opts)
-        # The attention's KV ring likewise: each ring step needs every rank's send / receive
-        # kernels, so one rank whose GPU is full of pending attention CTAs would stall the step
+        # The attention's KV exchange likewise: each exchange part needs every rank's send /
+        # receive kernels, so one rank whose GPU is full of pending attention CTAs would stall it
         # for all ranks.
         ring_group = dist.new_group(list(range(world)), backend="nccl", pg_options=opts)
     else:
@@ -997,7 +997,7 @@ def bench_cp_block(args, dev, stream, max_over_ranks, barrier, world, rank) -> d
             "scaling": "strong",
             "config": "BASELINE config 5 prefill: 1 x 131072 tokens over the ranks; 1 gated GQA "
                       "layer (config 3 shapes) context-parallel with zig-zag chunks and an NCCL "
-                      "ring KV exchange; 3 Gated DeltaNet layers (config 4 shapes) as a state "
+                      "direct KV exchange; 3 Gated DeltaNet layers (config 4 shapes) as a state "
                       "hand-off wavefront over contiguous segments",
             "attention": {"ms": attn_ms, "tflops_per_gpu": a_tf / world, "flops": a_flops,
                           "frac_of_peak_per_gpu": a_tf / world / pk["bf16_tflops"],
