@@ -349,9 +349,13 @@ int miso_deltanet_step_batched(const miso_deltanet_step_batched_params* p, void*
  * kernels/deltanet_step.hpp:146-273, launched at src/engine/deltanet.hip:112), computed with the
  * chunked gated delta rule (chunk 64; kernels/deltanet_chunk.hpp:3-9) instead of token by token.
  * Outputs agree with the recurrence to ~1e-4 relative (fp16 operands, fp32 accumulation and
- * state). Requires conv_in != conv_out, qkv and state 16-byte aligned, qkv_stride a multiple of 4,
- * and `scratch` (256-byte aligned) of at least miso_deltanet_prefill_tc_scratch_bytes(n) bytes,
- * which the call overwrites. */
+ * state). Requires conv_in != conv_out, qkv, z, norm_w, out and state 16-byte aligned, qkv_stride
+ * and zab_stride multiples of 4, and `scratch` (256-byte aligned) of at least
+ * miso_deltanet_prefill_tc_scratch_bytes(n) bytes, which the call overwrites. For n > 2048 the
+ * call runs the sequence in pieces of 2048 tokens on three internal streams of the device (fork
+ * from and join into `stream` by events, so the call stays ordered on `stream`); the first such
+ * call on a device creates those streams and events, so it should come before any stream
+ * capture, and calls from several host threads are serialised while they enqueue. */
 size_t miso_deltanet_prefill_tc_scratch_bytes(unsigned n);
 int miso_deltanet_prefill_tc(const miso_deltanet_seq_params* p, void* scratch, size_t scratch_bytes,
                              void* stream);
