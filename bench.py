@@ -715,7 +715,8 @@ def bench_deltanet_step(args, dev, stream, max_over_ranks, barrier, world) -> di
 
 
 DN_PREFILL_T = 8192
-DN_PIECES = -(-(DN_PREFILL_T // 64) // 32)  # pieces of 32 chunks per miso_deltanet_prefill_tc call
+# pieces per miso_deltanet_prefill_tc call: 16 chunks, then 32 each (the last one the remainder)
+DN_PIECES = 1 + -(-(DN_PREFILL_T // 64 - 16) // 32)
 # Algorithmic FLOPs of the chunked rule per (V head, chunk of 64): 2 (3 C d^2 + 3 C^2 d)
 # = 9.44 MFLOP (QK^T / KK^T, the UT-transform products, S updates), 32 heads x T / 64 chunks.
 DN_PREFILL_FLOPS_PER_HEAD_CHUNK = 2.0 * (3 * 64 * 128 * 128 + 3 * 64 * 64 * 128)
@@ -777,8 +778,8 @@ def bench_deltanet_prefill(args, dev, stream, max_over_ranks, barrier, world) ->
             "unit": "tokens/s", "ms_per_step": ms, "n_tokens": T,
             "config": "BASELINE config 4a: 1 x 8192 tokens per GPU, 16 K / 32 V heads, d 128, "
                       "chunk 64, bf16-valued inputs, zero initial state; fp16 hi/lo tensor "
-                      "operands, fp32 accumulation and state; one call per step = 4 pieces of "
-                      "2048 tokens x 3 launches (per-chunk records, state recurrence, gated "
+                      "operands, fp32 accumulation and state; one call per step = 5 pieces "
+                      "(1024, 3 x 2048, 1024 tokens) x 3 launches (per-chunk records, state recurrence, gated "
                       "norm) on three streams",
             "flops_per_step": flops, "tflops": tflops, "bytes_per_step": nbytes,
             "gbs": nbytes / (ms * 1e-3) / 1e9,

@@ -352,7 +352,7 @@ int miso_deltanet_step_batched(const miso_deltanet_step_batched_params* p, void*
  * state). Requires conv_in != conv_out, qkv, z, norm_w, out and state 16-byte aligned, qkv_stride
  * and zab_stride multiples of 4, and `scratch` (256-byte aligned) of at least
  * miso_deltanet_prefill_tc_scratch_bytes(n) bytes, which the call overwrites. For n > 2048 the
- * call runs the sequence in pieces of 2048 tokens on three internal streams of the device (fork
+ * call runs the sequence in pieces (1024 tokens, then 2048 each) on three internal streams of the device (fork
  * from and join into `stream` by events, so the call stays ordered on `stream`); the first such
  * call on a device creates those streams and events, so it should come before any stream
  * capture, and calls from several host threads are serialised while they enqueue. */

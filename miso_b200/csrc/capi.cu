@@ -92,6 +92,7 @@ DeviceInfo g_dev[kMaxDevices];
 // (the events are reused from call to call).
 constexpr int kDnMaxPieces = 64;
 constexpr unsigned kDnPieceChunks = 32;  // chunks of 64 tokens per piece (8, 16, 64 measured slower)
+constexpr unsigned kDnFirstPieceChunks = 16;  // the first piece
 struct DnPipe {
   std::once_flag once;
   int status = MISO_OK;
@@ -798,8 +799,11 @@ int dn_prefill_tc(const miso_deltanet_seq_params* p, void* scratch, size_t scrat
     return st;
   std::lock_guard<std::mutex> lock(q->mu);
   unsigned per = kDnPieceChunks;
-  if ((nc + per - 1) / per > unsigned(kDnMaxPieces))
-    per = (nc + kDnMaxPieces - 1) / kDnMaxPieces;
+  if ((nc + per - 1) / per + 1 > unsigned(kDnMaxPieces))
+    per = (nc + kDnMaxPieces - 2) / (kDnMaxPieces - 1);
+  // The first piece runs alone (nothing to overlap it with): a shorter one starts the chain
+  // sooner.
+  const unsigned first = kDnFirstPieceChunks < per ? kDnFirstPieceChunks : per;
   fa.ahead = unsigned(d->sms) > unsigned(pf::kVHeads) ? unsigned(d->sms) - pf::kVHeads : 1u;
   fa.per = per;
   auto ok = [](cudaError_t e) { return e == cudaSuccess ? MISO_OK : static_cast<int>(e); };
@@ -808,8 +812,9 @@ int dn_prefill_tc(const miso_deltanet_seq_params* p, void* scratch, size_t scrat
       (st = ok(cudaStreamWaitEvent(q->chain, q->fork, 0))) != MISO_OK ||
       (st = ok(cudaStreamWaitEvent(q->gate, q->fork, 0))) != MISO_OK)
     return st;
-  for (unsigned k = 0, c0 = 0; c0 < nc; ++k, c0 += per) {
-    const unsigned cnt = nc - c0 < per ? nc - c0 : per;
+  for (unsigned k = 0, c0 = 0, cnt = 0; c0 < nc; ++k, c0 += cnt) {
+    const unsigned want = k == 0 ? first : per;
+    cnt = nc - c0 < want ? nc - c0 : want;
     if ((st = front(q->front, c0, cnt)) != MISO_OK ||
         (st = ok(cudaEventRecord(q->front_done[k], q->front))) != MISO_OK ||
         (st = ok(cudaStreamWaitEvent(q->chain, q->front_done[k], 0))) != MISO_OK ||
