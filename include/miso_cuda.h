@@ -193,11 +193,14 @@ unsigned miso_attn_prefill_items(unsigned n);
 int miso_attn_prep(const miso_attn_prep_params* p, void* stream);
 /* attn_prep_batch_kernel<256><<<n * 18, 256>>>, src/engine/attention.hip:140. */
 int miso_attn_prep_batch(const miso_attn_prep_batch_params* p, void* stream);
-/* attn_split_kernel<256><<<(n_splits, 2), 256>>>, src/engine/attention.hip:106. */
+/* attn_split_kernel<256><<<(n_splits, 2), 256>>>, src/engine/attention.hip:106. q, k_cache and
+ * v_cache 16-byte aligned. */
 int miso_attn_split(const miso_attn_split_params* p, void* stream);
 /* attn_combine_kernel<64, true, 4><<<64, 64>>>, src/engine/attention.hip:109. */
 int miso_attn_combine(const miso_attn_combine_params* p, void* stream);
-/* attn_prefill_kernel<256><<<attn_prefill_items(n), 256>>>, src/engine/attention.hip:144. */
+/* attn_prefill_kernel<256><<<attn_prefill_items(n), 256>>>, src/engine/attention.hip:144. q,
+ * k_cache and v_cache 16-byte aligned (MISO_ERR_INVALID otherwise). A token's result does not
+ * depend on how the prompt is cut into calls (bitwise). */
 int miso_attn_prefill(const miso_attn_prefill_params* p, void* stream);
 /* deltanet_step_kernel<256><<<32, 256>>>, src/engine/deltanet.hip:79. */
 int miso_deltanet_step(const miso_deltanet_step_params* p, void* stream);

@@ -307,7 +307,8 @@ int miso_attn_prep_batch(const miso_attn_prep_batch_params* p, void* stream) {
 int miso_attn_split(const miso_attn_split_params* p, void* stream) {
   if (p == nullptr || p->q == nullptr || p->k_cache == nullptr || p->v_cache == nullptr ||
       p->part_m == nullptr || p->part_l == nullptr || p->part_o == nullptr || p->n_splits == 0 ||
-      p->len == 0 || p->len > p->max_ctx || p->n_splits > 65535 || !aligned16(p->k_cache) ||
+      p->len == 0 || p->len > p->max_ctx || p->n_splits > 65535 || !aligned16(p->q) ||
+      !aligned16(p->k_cache) ||
       !aligned16(p->v_cache) || !aligned16(p->part_o))
     return MISO_ERR_INVALID;
   k::attn_split_kernel<256><<<dim3(p->n_splits, 2), 256, 0, as_stream(stream)>>>(
@@ -327,7 +328,7 @@ int miso_attn_combine(const miso_attn_combine_params* p, void* stream) {
 int miso_attn_prefill(const miso_attn_prefill_params* p, void* stream) {
   if (p == nullptr || p->q == nullptr || p->qg == nullptr || p->k_cache == nullptr ||
       p->v_cache == nullptr || p->core == nullptr || uint64_t(p->pos0) + p->n > p->max_ctx ||
-      !aligned16(p->v_cache))
+      !aligned16(p->q) || !aligned16(p->k_cache) || !aligned16(p->v_cache))
     return MISO_ERR_INVALID;
   if (p->n == 0)
     return MISO_OK;

@@ -342,6 +342,34 @@ def test_prefill_matches_fp64(pos0, n):
     assert rel_per_head(core.cpu().numpy(), ref) <= 1e-5
 
 
+@pytest.mark.parametrize("cuts", [(13,), (1, 2, 3), (4, 8, 29), (16, 17)])
+def test_prefill_does_not_depend_on_how_the_prompt_is_cut(cuts):
+    """A token's core row is bitwise the same whether the prompt goes in one call or in several
+    (each later call at pos0 = the tokens already cached), as the engine's chunked prefill and the
+    reference's test_prefill expect: the row depends on the token's keys alone, not on the 4-token
+    block it shares or the slabs the other tokens of the call reach."""
+    n, pos0 = 37, 5
+    max_ctx = pos0 + n
+    rng = np.random.RandomState(77 + len(cuts))
+    q = T((2.0 * rng.standard_normal((n, 16, 256))).astype(np.float32))
+    qg = T(rng.standard_normal((n, 16, 512)).astype(np.float32))
+    k = T(rng.standard_normal((2, max_ctx, 256)).astype(np.float16))
+    v = T(rng.standard_normal((2, max_ctx, 256)).astype(np.float16))
+
+    def run(a, b, core):
+        A.attn_prefill(capi.AttnPrefillParams(ptr(q[a]), ptr(qg[a]), ptr(k), ptr(v), ptr(core[a]),
+                                              pos0 + a, b - a, max_ctx, 16 * 512))
+
+    whole = torch.full((n, 16, 256), -1.0, device=DEV)
+    run(0, n, whole)
+    parts = torch.full_like(whole, -2.0)
+    edges = [0, *cuts, n]
+    for a, b in zip(edges, edges[1:]):
+        run(a, b, parts)
+    torch.cuda.synchronize()
+    assert torch.equal(whole.view(torch.int32), parts.view(torch.int32))
+
+
 def test_engine_decode_sequence_matches_oracle():
     """attention_decode_core token by token (prep -> split -> combine), as the engine drives it."""
     rng = np.random.RandomState(4)
