@@ -85,11 +85,12 @@ struct TokenShared {
 // state s (rows 16w + i, columns 4 lane + c), gated RMSNorm. Expects sh.q / sh.k / sh.v to hold
 // the SiLU'd conv outputs (written before the call, no barrier needed in between: the first
 // statement is a barrier). Writes out[col] for col in [0, 128) from threads 0..127.
-// beta_in / a_in are the raw b[h] / a[h] inputs of this token.
+// beta_in / a_in are the raw b[h] / a[h] inputs of this token; norm_w_t / z_t are norm_w[t] and
+// this token's gate z[t] for threads t < 128 (ignored above), passed as values so that a caller
+// can load them ahead of the token.
 __device__ __forceinline__ void token_update(TokenShared& sh, float4 (&s)[16], float beta_in,
                                              float a_in, float ssm_a, float dt_bias,
-                                             const float* norm_w, const float* z, float eps,
-                                             float* out) {
+                                             float norm_w_t, float z_t, float eps, float* out) {
   using namespace deltanet_detail;
   const unsigned t = threadIdx.x, w = t / 32, lane = t % 32;
   __syncthreads();
@@ -155,7 +156,7 @@ __device__ __forceinline__ void token_update(TokenShared& sh, float4 (&s)[16], f
   __syncthreads();
   if (t < kDim) {
     const float r = rsqrtf((sh.red[0] + sh.red[1] + sh.red[2] + sh.red[3]) / kDim + eps);
-    out[t] = oh * r * norm_w[t] * silu(z[t]);
+    out[t] = oh * r * norm_w_t * silu(z_t);
   }
 }
 
@@ -196,8 +197,9 @@ __device__ void deltanet_step_op(const DeltaNetStepParams& p, unsigned first, un
     } else {
       sh.k[t - kDim] = conv_step(p, kKHeads * kDim + kh * kDim + (t - kDim), own_qk);
     }
-    dn_detail::token_update(sh, s, p.b[h], p.a[h], p.ssm_a[h], p.dt_bias[h], p.norm_w,
-                            p.z + h * kDim, p.eps, p.out + h * kDim);
+    dn_detail::token_update(sh, s, p.b[h], p.a[h], p.ssm_a[h], p.dt_bias[h],
+                            t < kDim ? p.norm_w[t] : 0.0f, t < kDim ? p.z[h * kDim + t] : 0.0f,
+                            p.eps, p.out + h * kDim);
     dn_detail::store_state(s, S);
     __syncthreads();
   }
@@ -268,22 +270,39 @@ __device__ void seq_body(const DeltaNetSeqParams& p, const SeqSinks& out, unsign
     const float* S = p.state + std::size_t{h} * kDim * kDim;
     float4 s[16];
     dn_detail::load_state(s, S);
-    for (unsigned tok = 0; tok < p.n; ++tok) {
+    const float nw = t < kDim ? p.norm_w[t] : 0.0f;
+    const float ssm_a_h = p.ssm_a[h], dt_bias_h = p.dt_bias[h];
+    // A token's own inputs (conv inputs x0 / x1, b, a and the gate z[t]) are loaded one token
+    // ahead, so their memory latency overlaps the previous token's update; the arithmetic is
+    // unchanged.
+    float nx0 = 0.0f, nx1 = 0.0f, nb = 0.0f, na = 0.0f, nz = 0.0f;
+    auto load_inputs = [&](unsigned tok) {
       const float* x = p.qkv + std::size_t{tok} * p.qkv_stride;
-      const float x0 = x[c0];
+      const std::size_t zrow = std::size_t{tok} * p.zab_stride;
+      nx0 = x[c0];
+      if (t < kDim) {
+        nx1 = x[c1];
+        nz = p.z[zrow + h * kDim + t];
+      }
+      nb = p.b[zrow + h];
+      na = p.a[zrow + h];
+    };
+    if (p.n > 0)
+      load_inputs(0);
+    for (unsigned tok = 0; tok < p.n; ++tok) {
+      const float x0 = nx0, x1 = nx1, b_in = nb, a_in = na, z_t = nz;
+      if (tok + 1 < p.n)
+        load_inputs(tok + 1);
       const float y0 = silu(w0[0] * h0[0] + w0[1] * h0[1] + w0[2] * h0[2] + w0[3] * x0);
       h0[0] = h0[1], h0[1] = h0[2], h0[2] = x0;
       if (t < kDim) {
-        const float x1 = x[c1];
         const float y1 = silu(w1[0] * h1[0] + w1[1] * h1[1] + w1[2] * h1[2] + w1[3] * x1);
         h1[0] = h1[1], h1[1] = h1[2], h1[2] = x1;
         sh.q[t] = y0, sh.v[t] = y1;
       } else {
         sh.k[t - kDim] = y0;
       }
-      const std::size_t zrow = std::size_t{tok} * p.zab_stride;
-      dn_detail::token_update(sh, s, p.b[zrow + h], p.a[zrow + h], p.ssm_a[h], p.dt_bias[h],
-                              p.norm_w, p.z + zrow + h * kDim, p.eps,
+      dn_detail::token_update(sh, s, b_in, a_in, ssm_a_h, dt_bias_h, nw, z_t, p.eps,
                               p.out + std::size_t{tok} * kOut + h * kDim);
       if (out.state_ckpt != nullptr)
         dn_detail::store_state(s, out.state_ckpt + tok * kStateFloats + std::size_t{h} * kDim * kDim);
