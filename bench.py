@@ -562,7 +562,7 @@ PREFILL_N = 8192
 DECODE_TRAFFIC_PER_ALGORITHMIC_BYTE = (257.0 + 6.3) / 256.8
 # ncu DRAM bytes (read + write) of one full-size launch (profiles/prefill_kernel_8k_ncu.md,
 # profiles/deltanet_prefill_tc_8k_ncu.md).
-PREFILL_8K_TRAFFIC = (221.3 + 101.5) * 1e6
+PREFILL_8K_TRAFFIC = (237.3 + 101.1) * 1e6
 # DRAM bytes (read + write inside each launch) of the three kernels of a piece of 1024 tokens
 # (front 49.9 + 15.8 MB, chain 69.3 + 3.1 MB, gate 33.6 + 0.0 MB; ncu, caches flushed before each
 # launch), times the 8 such token ranges of a call at 8192 tokens (every byte is per token: the
