@@ -86,14 +86,17 @@ def test_step_matches_oracle():
     assert rel(st.cpu().numpy(), st64[0]) < 1e-5
 
 
-def test_sequence_equals_steps_bitwise():
-    x = chunk_test_inputs(7)
+@pytest.mark.parametrize("n", [7, 37])
+def test_sequence_equals_steps_bitwise(n):
+    """The sequence kernel works in groups of 8 tokens: 7 is one partial group, 37 four whole
+    groups and a partial one. Each must carry exactly the bits of n single steps."""
+    x = chunk_test_inputs(n)
     out_seq, st_seq, co_seq = run_seq(x)
     d = {k: T(x[k]) for k in ("conv_w", "ssm_a", "dt", "norm_w")}
     conv = [T(x["conv_in"]), torch.empty((8192, 3), device=DEV)]
     st = T(x["state"])
     outs = []
-    for t in range(7):
+    for t in range(n):
         qkv, z, a, b = (T(x[k][t]) for k in ("qkv", "z", "a", "b"))
         out = torch.empty(4096, device=DEV)
         DN.step(capi.DeltaNetStepParams(ptr(qkv), ptr(z), ptr(a), ptr(b), ptr(d["conv_w"]),
@@ -103,7 +106,7 @@ def test_sequence_equals_steps_bitwise():
     torch.cuda.synchronize()
     assert np.array_equal(np.stack(outs).view(np.uint32), out_seq.view(np.uint32))
     assert np.array_equal(st.cpu().numpy().view(np.uint32), st_seq.view(np.uint32))
-    assert np.array_equal(conv[1].cpu().numpy(), co_seq)
+    assert np.array_equal(conv[n % 2].cpu().numpy(), co_seq)  # the last step wrote conv[n % 2]
 
 
 def test_sequence_matches_transformers_golden_and_oracle():
